@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""Benchmark of the farthest-point-sampling engine (one JSON line on rank 0).
+
+Metric: FPS samples/sec (whole box) at 1/2/4/8 B200; ms per
+122,880 -> 16,384 scan.
+
+Default workload: every rank samples one synthetic
+64-beam LiDAR scan (122,880 points -> 16,384 samples, range x,y in [-80, 80],
+z in [-3, 3], 32 x 32 x 8 blocks) per step, its own scan (seed = rank).  The
+path shards whole clouds across GPUs with no collective, so scaling is weak:
+`value` = samples of all ranks / the slowest rank's time.  `--workload c5`
+runs the 256-scan batch split over the ranks instead (strong scaling).
+
+  value   device-resident: the scan is in HBM before timing starts; each step
+          is one nsfps_fps_device call (binning, sort, leaf build, sampling
+          loop, epilogue) timed with CUDA events on the launching stream, with
+          a 256 MiB L2 flush outside the timed window between steps.
+  e2e     the same through nsfps_fps with HOST buffers: the H2D copy of the
+          points and the D2H copy of the indices are inside the timed region.
+  roofline  for the sampling-loop kernel: algorithmic bytes = 12 N + 20 sum_i
+          u_i (u_i = points in the buckets the reference updates at step i,
+          counted by the kernel itself) over the kernel's event-timed duration,
+          against the measured HBM copy bandwidth.
+  cpu_baseline  the reference's yuezu_fps() compiled from its own sources
+          (oracle/_ref), timed on this host on a bounded sample.
+
+`--impl reference` times the reference CPU implementation alone on the same
+workload with the host threads it can use (rank 0 only under torchrun).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from ns_fps_b200 import dist as D  # noqa: E402
+from ns_fps_b200 import synthetic as S  # noqa: E402
+
+METRIC = "FPS samples/sec (whole box) at 1/2/4/8 B200; ms per 122,880→16,384 scan"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_clouds(name: str, rank: int, world: int):
+    """The clouds this rank samples every step, and a description."""
+    cfg = S.CONFIGS[name]
+    if name in ("c1", "c2", "c4"):
+        clouds = S.make(name, seed=rank, count=1)  # weak scaling: one cloud per rank
+        scaling = "weak"
+        per = 1
+    else:
+        total = cfg.clouds
+        idx = D.shard_indices(total, rank, world)
+        if name == "c3":
+            clouds = [S.sphere_cube_cloud(cfg.n, seed=i) for i in idx]
+        else:
+            clouds = [S.lidar_scan(i) for i in idx]
+        scaling = "strong"
+        per = len(idx)
+    return cfg, clouds, scaling, per
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes of one sampling-loop launch from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "loop_kernel_traffic.json")
+    try:
+        with open(path) as f:
+            t = json.load(f)
+        return t.get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+def cpu_baseline(cfg, clouds, threads: int):
+    """The reference's yuezu_fps() (oracle/_ref) on a bounded sample: one
+    whole cloud per thread, `threads` threads (1 for a single cloud)."""
+    import oracle
+    if not oracle.have_ref():
+        sample = clouds[: max(1, threads)]
+        t0 = time.perf_counter()
+        n = 0
+        for c in sample:
+            n += len(oracle.fps(c, cfg.k, cfg.rng, cfg.blocks))
+        dt = time.perf_counter() - t0
+        return {"value": n / dt, "unit": "samples/s", "cores": 1, "kind": "port",
+                "sample": f"{len(sample)} cloud(s) of {cfg.n} points -> {cfg.k} samples, "
+                          f"{dt:.2f} s"}
+    sample = clouds[: max(1, threads)]
+    outs, secs = oracle.ref_fps_many(sample, cfg.k, cfg.rng, cfg.blocks, threads=len(sample))
+    n = sum(len(o) for o in outs)
+    return {"value": n / secs, "unit": "samples/s", "cores": len(sample), "kind": "reference",
+            "sample": f"{len(sample)} whole cloud(s) of {cfg.n} points -> {cfg.k} samples "
+                      f"on {len(sample)} thread(s), {secs:.2f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference CPU implementation alone."""
+    rank, _, world = D.env_rank()
+    if rank != 0:
+        return 0
+    import oracle
+    cfg, clouds, scaling, per = workload_clouds(args.workload, 0, 1)
+    if args.workload in ("c3", "c5"):
+        clouds = clouds[: max(1, min(len(clouds), os.cpu_count() or 1))]
+    threads = len(clouds)
+    times, n_samples = [], 0
+    for s in range(args.warmup + args.steps):
+        if oracle.have_ref():
+            outs, secs = oracle.ref_fps_many(clouds, cfg.k, cfg.rng, cfg.blocks, threads=threads)
+            kind = "reference"
+        else:
+            t0 = time.perf_counter()
+            outs = [oracle.fps(c, cfg.k, cfg.rng, cfg.blocks) for c in clouds]
+            secs = time.perf_counter() - t0
+            kind, threads = "port", 1
+        if s >= args.warmup:
+            times.append(secs)
+            n_samples += sum(len(o) for o in outs)
+    total = sum(times)
+    value = n_samples / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "clouds_per_step": len(clouds), "points": cfg.n,
+                   "k": cfg.k, "blocks": list(cfg.blocks)},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": kind,
+                         "sample": f"{len(clouds)} whole cloud(s) per step, {threads} thread(s)"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    rank, local, world = D.env_rank()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    D.init("nccl", timeout_s=300)
+    from ns_fps_b200 import capi
+
+    cfg, clouds, scaling, per = workload_clouds(args.workload, rank, world)
+    k = cfg.k
+    offsets = np.zeros(len(clouds) + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum([c.shape[0] for c in clouds])
+    packed = np.ascontiguousarray(np.concatenate(clouds, axis=0).astype(np.float32))
+    d_xyz = torch.from_numpy(packed).to(dev)
+    d_out = torch.empty(len(clouds) * k, dtype=torch.int64, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ranges = (cfg.rng, cfg.blocks)
+
+    def step():
+        return capi.fps_device(d_xyz.data_ptr(), offsets, k, ranges, False, d_out.data_ptr(),
+                               stream.cuda_stream)
+
+    capi.set_profiling(True)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    D.barrier(local)
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    loop_ms, ref_pts, evals, launches, samples = 0.0, 0, 0, 0, 0
+    with ClockSampler(local) as clk:
+        for s in range(args.steps):
+            flush.zero_()  # L2 flush outside the timed window
+            ev[s][0].record(stream)
+            lens = step()
+            ev[s][1].record(stream)
+            prof = capi.last_profile()
+            loop_ms += prof.loop_ms
+            ref_pts += prof.ref_points_updated
+            evals += prof.points_evaluated
+            launches += prof.launches
+            samples += sum(lens)
+        torch.cuda.synchronize(dev)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    my_ms = float(sum(step_ms))
+    D.barrier(local)
+
+    # ---- end to end through the C ABI with host buffers
+    host = [np.ascontiguousarray(c) for c in clouds]
+    pinned = [torch.from_numpy(c).pin_memory() for c in host]
+    e2e_times = []
+    for s in range(max(1, args.steps // 2) + 1):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        if len(pinned) == 1:
+            out = capi.fps(pinned[0].numpy(), k, cfg.rng, cfg.blocks, device=local)
+            e2e_n = len(out)
+        else:
+            outs = capi.fps_batched([p.numpy() for p in pinned], k, cfg.rng, cfg.blocks,
+                                    devices=(local,))
+            e2e_n = sum(len(o) for o in outs)
+        dt = time.perf_counter() - t0
+        if s > 0:
+            e2e_times.append(dt)
+    e2e_s = float(np.mean(e2e_times))
+
+    # ---- aggregate over ranks (max of times, sum of work)
+    mx = D.max_over_ranks([my_ms, e2e_s], device=dev)
+    sm = D.sum_over_ranks([samples, e2e_n, ref_pts, len(clouds)], device=dev)
+    total_ms, e2e_max = mx
+    all_samples, all_e2e, _, _ = sm
+
+    result = None
+    if rank == 0:
+        value = all_samples / (total_ms / 1e3)
+        e2e_value = all_e2e / e2e_max
+        # roofline of the sampling loop kernel on this rank
+        n_pts = int(offsets[-1])
+        alg_bytes = 12.0 * n_pts * args.steps + 20.0 * ref_pts
+        achieved = alg_bytes / (loop_ms / 1e3) / 1e9
+        peak, peak_kind = measured_peaks()
+        traffic = profiled_traffic(args.workload)
+        iters = samples / max(len(clouds), 1) / args.steps
+        result = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "clouds_per_gpu": len(clouds), "points": cfg.n,
+                       "k": k, "blocks": list(cfg.blocks), "range": list(cfg.rng),
+                       "l2": "256 MiB flush between steps, outside the timed window"},
+            "ms_per_scan": my_ms / args.steps / max(len(clouds), 1) if per == 1 else None,
+            "us_per_iteration": (loop_ms / args.steps) * 1e3 / max(iters, 1),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "kernel": "fps_loop_cluster",
+                         "algorithmic_bytes_per_launch": alg_bytes / args.steps,
+                         "kernel_ms_per_launch": loop_ms / args.steps,
+                         "points_evaluated_per_launch": evals / args.steps},
+            "e2e": {"value": e2e_value, "unit": "samples/s",
+                    "h2d_bytes_per_step": int(12 * n_pts),
+                    "d2h_bytes_per_step": int(8 * k * len(clouds) + 8 * len(clouds))},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            cfgc = S.CONFIGS[args.workload]
+            threads = 1 if per == 1 else min(len(clouds), os.cpu_count() or 1)
+            result["cpu_baseline"] = cpu_baseline(cfgc, clouds, threads)
+    D.barrier(local)
+    D.finalize()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

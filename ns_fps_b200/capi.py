@@ -1,0 +1,138 @@
+"""ctypes binding of the engine's C ABI (include/nsfps.h).
+
+This is the binding a Python integrator writes against libnsfps.so without
+the pybind11 module; bench.py and the tests use it to call the engine through
+its C ABI.  Every function raises RuntimeError with nsfps_last_error() when a
+call fails.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(ROOT, "ns_fps_b200", "libnsfps.so")
+HEADER = os.path.join(ROOT, "include", "nsfps.h")
+
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+
+class Range(ctypes.Structure):
+    _fields_ = [("min_x", ctypes.c_float), ("max_x", ctypes.c_float),
+                ("min_y", ctypes.c_float), ("max_y", ctypes.c_float),
+                ("min_z", ctypes.c_float), ("max_z", ctypes.c_float),
+                ("x_blocks", ctypes.c_uint32), ("y_blocks", ctypes.c_uint32),
+                ("z_blocks", ctypes.c_uint32)]
+
+
+class RangeInfo(ctypes.Structure):
+    _fields_ = [("inv_bs", ctypes.c_float * 3), ("block_size", ctypes.c_float * 3),
+                ("bits", ctypes.c_uint32 * 3), ("total_bits", ctypes.c_uint32),
+                ("total_blocks", ctypes.c_uint64)]
+
+
+class Profile(ctypes.Structure):
+    _fields_ = [("setup_ms", ctypes.c_float), ("loop_ms", ctypes.c_float),
+                ("total_ms", ctypes.c_float), ("launches", ctypes.c_uint32),
+                ("ctas_per_cloud", ctypes.c_uint32), ("mode", ctypes.c_uint32),
+                ("leaves", ctypes.c_uint32), ("ref_points_updated", ctypes.c_uint64),
+                ("points_evaluated", ctypes.c_uint64), ("iterations", ctypes.c_uint64)]
+
+
+OK, ERR_ARG, ERR_CUDA, ERR_OOM, ERR_TIMEOUT, ERR_UNSUPPORTED = range(6)
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} missing: run `python -m ns_fps_b200.build`")
+        _lib = ctypes.CDLL(LIB_PATH)
+        _lib.nsfps_last_error.restype = ctypes.c_char_p
+    return _lib
+
+
+def last_error() -> str:
+    return lib().nsfps_last_error().decode()
+
+
+def rng(bounds, blocks) -> Range:
+    return Range(*[float(v) for v in bounds], *[int(b) for b in blocks])
+
+
+def fps(points, k, bounds=None, blocks=(16, 16, 16), device=0):
+    """nsfps_fps; bounds None = compute_bbox(16^3) like fps(range=None)."""
+    p = np.ascontiguousarray(np.asarray(points, dtype=np.float32))
+    n = p.shape[0]
+    out = np.zeros(max(min(int(k), n), 1), dtype=np.uint64)
+    ln = ctypes.c_uint64(0)
+    r = rng(bounds, blocks) if bounds is not None else None
+    rc = lib().nsfps_fps(p.ctypes.data_as(_f32p), ctypes.c_uint64(n), ctypes.c_uint64(int(k)),
+                         ctypes.byref(r) if r is not None else None,
+                         out.ctypes.data_as(_u64p), ctypes.byref(ln), ctypes.c_int(device))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_fps rc={rc}: {last_error()}")
+    return out[:ln.value].copy()
+
+
+def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
+    cl = [np.ascontiguousarray(np.asarray(c, dtype=np.float32)) for c in clouds]
+    cnt = len(cl)
+    ptrs = (_f32p * cnt)(*[c.ctypes.data_as(_f32p) for c in cl])
+    ns = (ctypes.c_uint64 * cnt)(*[c.shape[0] for c in cl])
+    outs = [np.zeros(max(min(int(k), c.shape[0]), 1), dtype=np.uint64) for c in cl]
+    optrs = (_u64p * cnt)(*[o.ctypes.data_as(_u64p) for o in outs])
+    lens = (ctypes.c_uint64 * cnt)()
+    if per_cloud:
+        rs = (Range * cnt)(*[rng(b, bl) for b, bl in zip(bounds, blocks)])
+    else:
+        rs = (Range * 1)(rng(bounds, blocks))
+    devs = (ctypes.c_int * len(devices))(*devices)
+    rc = lib().nsfps_fps_batched(ptrs, ns, ctypes.c_uint64(cnt), ctypes.c_uint64(int(k)), rs,
+                                 ctypes.c_int(1 if per_cloud else 0), optrs, lens, devs,
+                                 ctypes.c_int(len(devices)))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_fps_batched rc={rc}: {last_error()}")
+    return [o[:lens[i]].copy() for i, o in enumerate(outs)]
+
+
+def set_profiling(on: bool):
+    lib().nsfps_set_profiling(ctypes.c_int(1 if on else 0))
+
+
+def last_profile() -> Profile:
+    p = Profile()
+    lib().nsfps_last_profile(ctypes.byref(p))
+    return p
+
+
+def header_functions():
+    """Names of the functions include/nsfps.h declares."""
+    import re
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"NSFPS_API\s+[^;()]*?\b(nsfps_\w+)\s*\(", txt)))
+
+
+def fps_device(d_xyz_ptr: int, offsets, k: int, ranges, per_cloud: bool, d_out_ptr: int,
+               stream_ptr: int = 0):
+    """nsfps_fps_device: clouds already in device memory (packed float32 xyz at
+    d_xyz_ptr, `offsets` = count + 1 point offsets), results to the device
+    buffer at d_out_ptr (count * k uint64).  `ranges` is one (bounds, blocks)
+    pair or a list of them.  Returns the per-cloud sample counts."""
+    count = len(offsets) - 1
+    offs = (ctypes.c_uint64 * (count + 1))(*[int(o) for o in offsets])
+    if per_cloud:
+        rs = (Range * count)(*[rng(b, bl) for b, bl in ranges])
+    else:
+        rs = (Range * 1)(rng(*ranges))
+    lens = (ctypes.c_uint64 * count)()
+    rc = lib().nsfps_fps_device(ctypes.c_void_p(d_xyz_ptr), offs, ctypes.c_uint64(count),
+                                ctypes.c_uint64(int(k)), rs, ctypes.c_int(1 if per_cloud else 0),
+                                ctypes.c_void_p(d_out_ptr), lens, ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_fps_device rc={rc}: {last_error()}")
+    return [int(v) for v in lens]

@@ -1,0 +1,857 @@
+// nsfps_capi.cu -- host side of the engine: the C ABI declared in
+// include/nsfps.h, SpaceRange arithmetic, per-device workspaces and streams,
+// and the orchestration of setup -> plan -> sampling loop -> epilogue.
+//
+// SpaceRange arithmetic restates make_range / make_uniform_range /
+// compute_bbox of the reference (src/yuezu_fps.cpp:7-161, :643-670) in
+// host float arithmetic (SSE, round-to-nearest, no contraction: this file is
+// compiled with -fmad=false and the host compiler's default
+// -ffp-contract=off for ISO C++ is forced by -Xcompiler -ffp-contract=off).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "nsfps.h"
+#include "nsfps_internal.cuh"
+#include "nsfps_kernels.h"
+
+namespace nsfps {
+
+// ------------------------------------------------------------------ errors
+namespace {
+thread_local std::string g_err;
+thread_local nsfps_profile g_prof;
+std::atomic<int> g_profiling{0};
+}  // namespace
+
+int set_error(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+void clear_error() { g_err.clear(); }
+
+#define NSFPS_CUDA(call)                                                      \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess)                                                    \
+      return set_error(e_ == cudaErrorMemoryAllocation ? NSFPS_ERR_OOM        \
+                                                       : NSFPS_ERR_CUDA,     \
+                       "%s failed: %s", #call, cudaGetErrorString(e_));      \
+  } while (0)
+
+// ------------------------------------------------------------- SpaceRange
+namespace {
+
+// src/yuezu_fps.cpp:45-50
+uint32_t calc_bits(uint32_t blocks) {
+  uint32_t bits = 0;
+  while (bits < 32 && (1u << bits) < blocks) ++bits;
+  return bits ? bits : 1;
+}
+
+// src/yuezu_fps.cpp:69-97: x->y->z over the common bits, then the remaining
+// bits of x, y, z in that order.
+void bit_positions(const uint32_t bits[3], uint8_t pos[3][kMaxAxisBits]) {
+  uint32_t bit = 0, np[3] = {0, 0, 0};
+  const uint32_t common = std::min({bits[0], bits[1], bits[2]});
+  const uint32_t maxb = std::max({bits[0], bits[1], bits[2]});
+  for (uint32_t i = 0; i < common; ++i)
+    for (int a = 0; a < 3; ++a) pos[a][np[a]++] = (uint8_t)bit++;
+  for (uint32_t i = common; i < maxb; ++i)
+    for (int a = 0; a < 3; ++a)
+      if (i < bits[a]) pos[a][np[a]++] = (uint8_t)bit++;
+}
+
+uint32_t spread(uint32_t v, uint32_t bits, const uint8_t *pos) {
+  uint32_t code = 0;
+  for (uint32_t k = 0; k < bits; ++k)
+    if (v & (1u << k)) code |= 1u << pos[k];
+  return code;
+}
+
+int check_range(const nsfps_range &r) {
+  const uint32_t b[3] = {r.x_blocks, r.y_blocks, r.z_blocks};
+  for (int a = 0; a < 3; ++a) {
+    if (b[a] == 0)
+      return set_error(NSFPS_ERR_ARG, "SpaceRange block counts must be >= 1 (got %u x %u x %u)",
+                       r.x_blocks, r.y_blocks, r.z_blocks);
+    if (b[a] > NSFPS_MAX_BLOCKS_PER_AXIS)
+      return set_error(NSFPS_ERR_UNSUPPORTED,
+                       "SpaceRange block count %u exceeds this engine's limit of %u per axis",
+                       b[a], NSFPS_MAX_BLOCKS_PER_AXIS);
+  }
+  return NSFPS_OK;
+}
+
+}  // namespace
+
+int range_to_dev(const nsfps_range &r, RangeDev *out, const char **why) {
+  (void)why;
+  int rc = check_range(r);
+  if (rc) return rc;
+  std::memset(out, 0, sizeof(*out));
+  const float mn[3] = {r.min_x, r.min_y, r.min_z};
+  const float mx[3] = {r.max_x, r.max_y, r.max_z};
+  const uint32_t b[3] = {r.x_blocks, r.y_blocks, r.z_blocks};
+  for (int a = 0; a < 3; ++a) {
+    volatile float span = mx[a] - mn[a];
+    volatile float bs = span / (float)b[a];
+    out->mn[a] = mn[a];
+    out->hi[a] = mx[a] - NSFPS_BOUNDARY_EPS;
+    out->inv_bs[a] = 1.0f / bs;
+    out->bsz[a] = bs;  // block_size_*() = (max - min) / blocks
+    out->blocks[a] = b[a];
+    out->bits[a] = calc_bits(b[a]);
+  }
+  out->total = b[0] * b[1] * b[2];
+  out->total_bits = out->bits[0] + out->bits[1] + out->bits[2];
+  uint8_t pos[3][kMaxAxisBits] = {};
+  bit_positions(out->bits, pos);
+  std::memcpy(out->pos, pos, sizeof(pos));
+  const uint32_t maxcode = spread(b[0] - 1, out->bits[0], pos[0]) |
+                           spread(b[1] - 1, out->bits[1], pos[1]) |
+                           spread(b[2] - 1, out->bits[2], pos[2]);
+  out->direct = maxcode < out->total ? 1u : 0u;
+  return NSFPS_OK;
+}
+
+// The ratio whose ceiling is the reference's cube half-width
+// (src/yuezu_fps.cpp:566-570): std::sqrt on a float, then a float division,
+// both correctly rounded on the host (sqrtss / divss).
+static inline float cube_ratio(float D, float bs) { return std::sqrt(D) / bs; }
+
+// Largest finite float D >= 0 for which `pred` holds, for a predicate that is
+// true at 0 and monotone (true, then false) in D.
+template <class F>
+static float max_true(F pred) {
+  uint32_t lo = 0, hi = 0x7f7fffffu;  // bit patterns of 0 and FLT_MAX
+  float f;
+  std::memcpy(&f, &hi, 4);
+  if (pred(f)) return f;
+  while (hi - lo > 1) {  // pred(lo) true, pred(hi) false
+    const uint32_t mid = lo + (hi - lo) / 2;
+    std::memcpy(&f, &mid, 4);
+    if (pred(f)) lo = mid; else hi = mid;
+  }
+  std::memcpy(&f, &lo, 4);
+  return f;
+}
+
+// For a positive finite block size the cube half-width is monotone in the
+// distance D, so it can be read from thresholds instead of being recomputed:
+// table a holds, for n = 0 .. blocks-2, the largest D with
+// ceil(sqrt(D) / bs) <= n (a half-width of blocks-1 or more covers the whole
+// axis), and ovf[a] the largest D whose ratio still converts to int.  The
+// device then needs no IEEE division or square root per iteration.
+void cube_thresholds(RangeDev &r, std::vector<float> &pool) {
+  r.fast_cube = 1;
+  for (int a = 0; a < 3; ++a)
+    if (!(r.bsz[a] > 0.0f) || !std::isfinite(r.bsz[a])) r.fast_cube = 0;
+  if (!r.fast_cube) return;
+  for (int a = 0; a < 3; ++a) {
+    const float bs = r.bsz[a];
+    r.tab_off[a] = (uint32_t)pool.size();
+    for (uint32_t n = 0; n + 1 < r.blocks[a]; ++n)
+      pool.push_back(max_true([&](float D) { return cube_ratio(D, bs) <= (float)n; }));
+    r.ovf[a] = max_true([&](float D) { return cube_ratio(D, bs) < 2147483648.0f; });
+  }
+}
+
+int range_info(const nsfps_range &r, nsfps_range_info *info) {
+  RangeDev d;
+  int rc = range_to_dev(r, &d, nullptr);
+  if (rc) return rc;
+  for (int a = 0; a < 3; ++a) {
+    info->inv_bs[a] = d.inv_bs[a];
+    info->block_size[a] = d.bsz[a];
+    info->bits[a] = d.bits[a];
+  }
+  info->total_bits = d.total_bits;
+  info->total_blocks = (uint64_t)r.x_blocks * r.y_blocks * r.z_blocks;
+  return NSFPS_OK;
+}
+
+// ------------------------------------------------------- device contexts
+namespace {
+
+struct DeviceCtx {
+  std::mutex mu;
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  void *ws = nullptr;
+  size_t ws_bytes = 0;
+  cudaEvent_t ev[4] = {};
+  bool ready = false;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceCtx g_ctx[kMaxDevices];
+std::mutex g_ctx_mu;
+
+int get_ctx(int device, DeviceCtx **out) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return set_error(NSFPS_ERR_CUDA, "no CUDA device available (%s)",
+                     e == cudaSuccess ? "0 devices" : cudaGetErrorString(e));
+  if (device < 0 || device >= count || device >= kMaxDevices)
+    return set_error(NSFPS_ERR_ARG, "device %d out of range (0..%d)", device, count - 1);
+  DeviceCtx *c = &g_ctx[device];
+  std::lock_guard<std::mutex> lk(g_ctx_mu);
+  if (!c->ready) {
+    NSFPS_CUDA(cudaSetDevice(device));
+    NSFPS_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    for (auto &ev : c->ev) NSFPS_CUDA(cudaEventCreate(&ev));
+    c->device = device;
+    c->ready = true;
+  }
+  *out = c;
+  return NSFPS_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Carves typed sub-buffers out of one allocation.
+struct Carver {
+  char *base;
+  size_t off = 0;
+  explicit Carver(void *b) : base((char *)b) {}
+  template <class T>
+  T *take(size_t count) {
+    off = align_up(off, 256);
+    T *p = (T *)(base ? base + off : nullptr);
+    off += sizeof(T) * std::max<size_t>(count, 1);
+    return p;
+  }
+};
+
+// One GPU job: clouds packed back to back.
+struct Job {
+  uint32_t n = 0;                 // total points
+  uint32_t B = 0;                 // clouds
+  uint32_t k = 0;
+  std::vector<uint32_t> poff;     // B + 1
+  std::vector<uint32_t> rid;      // B
+  std::vector<uint32_t> boff;     // B
+  std::vector<RangeDev> ranges;
+  std::vector<float> tabs;        // cube half-width thresholds of all ranges
+  uint64_t total_buckets = 0;
+  bool any_hashed = false;
+};
+
+struct Buffers {
+  float *xyz;
+  uint32_t *keys0, *vals0, *keys1, *vals1, *hist, *partial, *perm, *tmp0, *tmp1;
+  float4 *pts, *leaf_lo, *leaf_hi;
+  float *leaf_md;
+  uint32_t *leaf_start, *leaf_pre, *loff, *poff, *rid, *boff, *scalars, *plan, *cand;
+  RangeDev *ranges;
+  float *tabs;
+  uint32_t *out_rank, *out_count;
+  uint64_t *out;
+  unsigned long long *stats;
+};
+
+constexpr uint32_t kClusterCand[] = {1, 2, 4, 8, 16};
+constexpr int kNumCand = 5;
+
+size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
+  const size_t n = j.n;
+  const size_t tiles = (n + 4095) / 4096;
+  const size_t scan_len = std::max(n, 256 * tiles);
+  b.xyz = own_xyz ? c.take<float>(3 * n) : nullptr;
+  b.keys0 = c.take<uint32_t>(n);
+  b.vals0 = c.take<uint32_t>(n);
+  b.keys1 = c.take<uint32_t>(n);
+  b.vals1 = c.take<uint32_t>(n);
+  b.hist = c.take<uint32_t>(256 * tiles + 1);
+  b.partial = c.take<uint32_t>((scan_len + 4095) / 4096 + 2);
+  b.pts = c.take<float4>(n);
+  b.perm = c.take<uint32_t>(n);
+  b.tmp0 = c.take<uint32_t>(n);
+  b.tmp1 = c.take<uint32_t>(n);
+  b.leaf_start = c.take<uint32_t>(n + 1);
+  b.leaf_lo = c.take<float4>(n);
+  b.leaf_hi = c.take<float4>(n);
+  b.leaf_md = c.take<float>(n);
+  b.leaf_pre = j.any_hashed ? c.take<uint32_t>(n * kMaxPreimages) : nullptr;
+  b.loff = c.take<uint32_t>(j.B + 1);
+  b.poff = c.take<uint32_t>(j.B + 1);
+  b.rid = c.take<uint32_t>(j.B);
+  b.boff = c.take<uint32_t>(j.B);
+  b.ranges = c.take<RangeDev>(j.ranges.size());
+  b.tabs = c.take<float>(j.tabs.size());
+  b.scalars = c.take<uint32_t>(kScalarCount);
+  b.plan = c.take<uint32_t>(3 * kMaxCand);
+  b.cand = c.take<uint32_t>(kMaxCand);
+  b.out_rank = c.take<uint32_t>((size_t)j.B * j.k);
+  b.out_count = c.take<uint32_t>(j.B);
+  b.out = own_out ? c.take<uint64_t>((size_t)j.B * j.k) : nullptr;
+  b.stats = c.take<unsigned long long>(4);
+  return align_up(c.off, 256);
+}
+
+int ensure_ws(DeviceCtx *ctx, size_t bytes) {
+  if (ctx->ws_bytes >= bytes) return NSFPS_OK;
+  if (ctx->ws) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+  }
+  const size_t want = align_up(bytes + bytes / 4, 1 << 20);
+  cudaError_t e = cudaMalloc(&ctx->ws, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(NSFPS_ERR_OOM, "cudaMalloc of %zu bytes failed: %s", want,
+                     cudaGetErrorString(e));
+  }
+  ctx->ws_bytes = want;
+  return NSFPS_OK;
+}
+
+// Build a job from `count` clouds with point counts n[i]; ranges resolved.
+int build_job(const uint64_t *n, uint64_t count, uint64_t k,
+              const std::vector<nsfps_range> &ranges, const std::vector<uint32_t> &rid,
+              Job &j) {
+  uint64_t tot = 0;
+  j.B = (uint32_t)count;
+  j.k = (uint32_t)k;
+  j.poff.assign(count + 1, 0);
+  for (uint64_t i = 0; i < count; ++i) {
+    j.poff[i] = (uint32_t)tot;
+    tot += n[i];
+  }
+  if (tot >= (1ull << 31))
+    return set_error(NSFPS_ERR_UNSUPPORTED, "too many points in one call (%llu >= 2^31)",
+                     (unsigned long long)tot);
+  if (k >= (1ull << 31))
+    return set_error(NSFPS_ERR_UNSUPPORTED, "sample_count too large");
+  j.poff[count] = (uint32_t)tot;
+  j.n = (uint32_t)tot;
+  j.ranges.resize(ranges.size());
+  for (size_t r = 0; r < ranges.size(); ++r) {
+    int rc = range_to_dev(ranges[r], &j.ranges[r], nullptr);
+    if (rc) return rc;
+    if (!j.ranges[r].direct) j.any_hashed = true;
+    cube_thresholds(j.ranges[r], j.tabs);
+  }
+  if (j.tabs.empty()) j.tabs.push_back(0.0f);
+  j.rid = rid;
+  j.boff.assign(count, 0);
+  uint64_t b = 0;
+  for (uint64_t i = 0; i < count; ++i) {
+    j.boff[i] = (uint32_t)b;
+    b += j.ranges[rid[i]].total;
+    if (b > 0xffffffffull)
+      return set_error(NSFPS_ERR_UNSUPPORTED,
+                       "total number of buckets over the batch exceeds 2^32");
+  }
+  j.total_buckets = b;
+  return NSFPS_OK;
+}
+
+// Runs the whole pipeline for a job whose points are at d_xyz (device).
+// Writes B*k uint64 results to d_out and the B lengths to lens (host).
+int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_packed,
+            const float *const *h_clouds, const float *d_xyz_in, uint64_t *d_out_user,
+            std::vector<uint32_t> &lens, std::vector<uint64_t> *h_out) {
+  const bool own_xyz = d_xyz_in == nullptr;
+  const bool own_out = d_out_user == nullptr;
+  Buffers b{};
+  Carver dry(nullptr);
+  const size_t need = carve(dry, j, own_xyz, own_out, b);
+  int rc = ensure_ws(ctx, need);
+  if (rc) return rc;
+  Carver c(ctx->ws);
+  carve(c, j, own_xyz, own_out, b);
+  const bool prof = g_profiling.load() != 0;
+  uint32_t launches = 0;
+
+  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[0], st));
+  const float *d_xyz = d_xyz_in;
+  if (own_xyz) {
+    if (h_xyz_packed) {
+      NSFPS_CUDA(cudaMemcpyAsync(b.xyz, h_xyz_packed, sizeof(float) * 3 * (size_t)j.n,
+                                 cudaMemcpyHostToDevice, st));
+    } else {
+      for (uint32_t i = 0; i < j.B; ++i) {
+        const size_t cnt = j.poff[i + 1] - j.poff[i];
+        NSFPS_CUDA(cudaMemcpyAsync(b.xyz + 3 * (size_t)j.poff[i], h_clouds[i],
+                                   sizeof(float) * 3 * cnt, cudaMemcpyHostToDevice, st));
+      }
+    }
+    d_xyz = b.xyz;
+  }
+  NSFPS_CUDA(cudaMemcpyAsync(b.poff, j.poff.data(), 4 * (j.B + 1), cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.rid, j.rid.data(), 4 * j.B, cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.boff, j.boff.data(), 4 * j.B, cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.ranges, j.ranges.data(), sizeof(RangeDev) * j.ranges.size(),
+                             cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.tabs, j.tabs.data(), sizeof(float) * j.tabs.size(),
+                             cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.cand, kClusterCand, sizeof(kClusterCand),
+                             cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
+
+  SetupArgs sa{};
+  sa.n = j.n;
+  sa.B = j.B;
+  sa.max_key = (uint32_t)(j.total_buckets - 1);
+  sa.xyz = d_xyz;
+  sa.poff = b.poff;
+  sa.rid = b.rid;
+  sa.ranges = b.ranges;
+  sa.boff = b.boff;
+  sa.keys0 = b.keys0; sa.vals0 = b.vals0; sa.keys1 = b.keys1; sa.vals1 = b.vals1;
+  sa.hist = b.hist;
+  sa.partial = b.partial;
+  sa.pts = b.pts;
+  sa.perm = b.perm;
+  sa.tmp0 = b.tmp0; sa.tmp1 = b.tmp1;
+  sa.leaf_start = b.leaf_start;
+  sa.leaf_lo = b.leaf_lo; sa.leaf_hi = b.leaf_hi; sa.leaf_md = b.leaf_md;
+  sa.leaf_pre = b.leaf_pre;
+  sa.loff = b.loff;
+  sa.scalars = b.scalars;
+  sa.cand = b.cand;
+  sa.cand_host = kClusterCand;
+  sa.ncand = kNumCand;
+  sa.plan = b.plan;
+  NSFPS_CUDA(run_setup(sa, st, launches));
+
+  uint32_t hplan[3 * kMaxCand] = {};
+  uint32_t hscal[kScalarCount] = {};
+  NSFPS_CUDA(cudaMemcpyAsync(hplan, b.plan, sizeof(uint32_t) * 3 * kNumCand,
+                             cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaMemcpyAsync(hscal, b.scalars, sizeof(hscal), cudaMemcpyDeviceToHost, st));
+  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
+  NSFPS_CUDA(cudaStreamSynchronize(st));
+
+  // CTAs per cloud: the smallest count whose largest part fits in shared
+  // memory; then, while every cloud still gets its own SMs, keep doubling it
+  // until each thread owns a single leaf (less serial work per iteration).
+  const int max_smem = loop_max_smem();
+  uint32_t max_tab = 0;
+  for (const RangeDev &r : j.ranges)
+    if (r.fast_cube)
+      max_tab = std::max(max_tab, r.blocks[0] + r.blocks[1] + r.blocks[2] - 3);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+  auto fits = [&](int i, int &m, size_t &bytes) {
+    const uint32_t pts = hplan[3 * i], leaves = hplan[3 * i + 1], extra = hplan[3 * i + 2];
+    bytes = loop_smem_bytes(pts, leaves, extra, max_tab);
+    m = loop_leaves_per_thread(leaves);
+    return m > 0 && bytes <= (size_t)max_smem && pts <= 65535;
+  };
+  int pi = -1, m_sel = 0;
+  size_t bytes_sel = 0;
+  for (int i = 0; i < kNumCand; ++i) {
+    int m;
+    size_t bytes;
+    if (!fits(i, m, bytes)) continue;
+    if (pi < 0) {
+      pi = i; m_sel = m; bytes_sel = bytes;
+      continue;
+    }
+    if (m_sel == 1 || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
+    pi = i; m_sel = m; bytes_sel = bytes;
+  }
+  if (pi < 0)
+    return set_error(NSFPS_ERR_UNSUPPORTED,
+                     "cloud too large for the shared-memory-resident sampler "
+                     "(largest cloud part needs more than %d bytes at 16 CTAs)",
+                     max_smem);
+  LoopPlan plan{};
+  plan.mode = 0;
+  plan.P = kClusterCand[pi];
+  plan.leaves_per_thread = m_sel;
+  plan.direct = !j.any_hashed;
+  plan.smem_bytes = std::max<size_t>(bytes_sel, 16);
+
+  LoopArgs la{};
+  la.B = j.B;
+  la.k = j.k;
+  la.P = plan.P;
+  la.max_pts = hplan[3 * pi];
+  la.max_leaves = hplan[3 * pi + 1];
+  la.max_extra = hplan[3 * pi + 2];
+  la.max_tab = max_tab;
+  la.pts = b.pts;
+  la.leaf_start = b.leaf_start;
+  la.leaf_lo = b.leaf_lo;
+  la.leaf_hi = b.leaf_hi;
+  la.leaf_md = b.leaf_md;
+  la.leaf_pre = b.leaf_pre;
+  la.loff = b.loff;
+  la.poff = b.poff;
+  la.rid = b.rid;
+  la.ranges = b.ranges;
+  la.tabs = b.tabs;
+  la.out_rank = b.out_rank;
+  la.out_count = b.out_count;
+  la.scalars = b.scalars;
+  la.stats = b.stats;
+  la.timeout_ns = 2000000000ll;
+  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[2], st));
+  NSFPS_CUDA(run_loop(la, plan, st, launches));
+  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[3], st));
+  uint64_t *d_out = own_out ? b.out : d_out_user;
+  NSFPS_CUDA(run_epilogue(b.out_rank, b.out_count, b.perm, b.poff, j.B, j.k, d_out, st,
+                          launches));
+  lens.assign(j.B, 0);
+  unsigned long long hstats[4] = {};
+  NSFPS_CUDA(cudaMemcpyAsync(lens.data(), b.out_count, 4 * j.B, cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaMemcpyAsync(hscal, b.scalars, sizeof(hscal), cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaMemcpyAsync(hstats, b.stats, sizeof(hstats), cudaMemcpyDeviceToHost, st));
+  if (h_out) {
+    h_out->resize((size_t)j.B * j.k);
+    NSFPS_CUDA(cudaMemcpyAsync(h_out->data(), d_out, sizeof(uint64_t) * j.B * (size_t)j.k,
+                               cudaMemcpyDeviceToHost, st));
+  }
+  NSFPS_CUDA(cudaStreamSynchronize(st));
+  if (hscal[kScalarStatus] & kStatusTimeout)
+    return set_error(NSFPS_ERR_TIMEOUT, "sampling kernel: a bounded wait timed out");
+  if (hscal[kScalarStatus] & kStatusBadPlan)
+    return set_error(NSFPS_ERR_CUDA, "sampling kernel: partition exceeded its plan");
+
+  if (prof) {
+    nsfps_profile p{};
+    float ms = 0;
+    cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]);
+    p.setup_ms = ms;
+    cudaEventElapsedTime(&ms, ctx->ev[2], ctx->ev[3]);
+    p.loop_ms = ms;
+    cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[3]);
+    p.total_ms = ms;
+    p.launches = launches;
+    p.ctas_per_cloud = plan.P;
+    p.mode = (uint32_t)plan.mode;
+    p.leaves = hscal[kScalarLeaves];
+    p.ref_points_updated = hstats[0];
+    p.points_evaluated = hstats[1];
+    uint64_t iters = 0;
+    for (uint32_t l : lens) iters += l;
+    p.iterations = iters;
+    g_prof = p;
+  }
+  return NSFPS_OK;
+}
+
+int check_points(const float *xyz, uint64_t n) {
+  if (n && !xyz) return set_error(NSFPS_ERR_ARG, "points pointer is NULL");
+  return NSFPS_OK;
+}
+
+// compute_bbox (src/yuezu_fps.cpp:648-670), std::min/std::max semantics.
+nsfps_range bbox_of(const float *xyz, uint64_t n, uint32_t xb, uint32_t yb, uint32_t zb) {
+  nsfps_range r{};
+  if (n == 0) {
+    r = {0, 1, 0, 1, 0, 1, 1, 1, 1};
+    return r;
+  }
+  float mn[3] = {xyz[0], xyz[1], xyz[2]}, mx[3] = {xyz[0], xyz[1], xyz[2]};
+  for (uint64_t i = 0; i < n; ++i)
+    for (int a = 0; a < 3; ++a) {
+      const float v = xyz[3 * i + a];
+      mn[a] = (v < mn[a]) ? v : mn[a];
+      mx[a] = (mx[a] < v) ? v : mx[a];
+    }
+  const float eps = NSFPS_BOUNDARY_EPS;
+  r.min_x = mn[0] - eps; r.max_x = mx[0] + eps;
+  r.min_y = mn[1] - eps; r.max_y = mx[1] + eps;
+  r.min_z = mn[2] - eps; r.max_z = mx[2] + eps;
+  r.x_blocks = xb; r.y_blocks = yb; r.z_blocks = zb;
+  return r;
+}
+
+// Clouds handled without the GPU, exactly as yuezu_fps's early returns
+// (src/yuezu_fps.cpp:678-688): n == 0 or k == 0 -> [], k >= n -> 0..n-1.
+bool trivial(uint64_t n, uint64_t k) { return n == 0 || k == 0 || k >= n; }
+
+void fill_trivial(uint64_t n, uint64_t k, uint64_t *out, uint64_t *len) {
+  if (n == 0 || k == 0) { *len = 0; return; }
+  for (uint64_t i = 0; i < n; ++i) out[i] = i;
+  *len = n;
+}
+
+// Batched host-memory path on one device.
+int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
+                      const std::vector<uint64_t> &idx, uint64_t k,
+                      const std::vector<nsfps_range> &ranges,
+                      const std::vector<uint32_t> &rid_all, uint64_t *const *out,
+                      uint64_t *out_len) {
+  std::vector<uint64_t> gpu_idx;
+  for (uint64_t i : idx)
+    if (!trivial(n[i], k)) gpu_idx.push_back(i);
+  if (gpu_idx.empty()) return NSFPS_OK;
+  DeviceCtx *ctx = nullptr;
+  int rc = get_ctx(device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  NSFPS_CUDA(cudaSetDevice(device));
+  std::vector<uint64_t> gn;
+  std::vector<const float *> gc;
+  std::vector<uint32_t> grid;
+  for (uint64_t i : gpu_idx) {
+    gn.push_back(n[i]);
+    gc.push_back(clouds[i]);
+    grid.push_back(rid_all[i]);
+  }
+  Job j;
+  rc = build_job(gn.data(), gn.size(), k, ranges, grid, j);
+  if (rc) return rc;
+  std::vector<uint32_t> lens;
+  std::vector<uint64_t> hout;
+  rc = run_job(ctx, ctx->stream, j, nullptr, gc.data(), nullptr, nullptr, lens, &hout);
+  if (rc) return rc;
+  for (size_t c = 0; c < gpu_idx.size(); ++c) {
+    const uint64_t i = gpu_idx[c];
+    std::memcpy(out[i], hout.data() + c * (size_t)k, sizeof(uint64_t) * lens[c]);
+    out_len[i] = lens[c];
+  }
+  return NSFPS_OK;
+}
+
+}  // namespace
+}  // namespace nsfps
+
+// ======================================================================= C ABI
+using namespace nsfps;
+
+extern "C" {
+
+const char *nsfps_last_error(void) { return g_err.c_str(); }
+
+int nsfps_version(void) { return 100; }
+
+int nsfps_device_count(int *count) {
+  clear_error();
+  if (!count) return set_error(NSFPS_ERR_ARG, "count is NULL");
+  int c = 0;
+  cudaError_t e = cudaGetDeviceCount(&c);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *count = 0;
+    return set_error(NSFPS_ERR_CUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+  }
+  *count = c;
+  return NSFPS_OK;
+}
+
+int nsfps_make_range(float min_x, float max_x, float min_y, float max_y, float min_z,
+                     float max_z, uint32_t x_blocks, uint32_t y_blocks, uint32_t z_blocks,
+                     nsfps_range *out) {
+  clear_error();
+  if (!out) return set_error(NSFPS_ERR_ARG, "out is NULL");
+  *out = {min_x, max_x, min_y, max_y, min_z, max_z, x_blocks, y_blocks, z_blocks};
+  return NSFPS_OK;
+}
+
+int nsfps_make_uniform_range(float min_x, float max_x, float min_y, float max_y,
+                             float min_z, float max_z, uint32_t blocks_per_dim,
+                             nsfps_range *out) {
+  return nsfps_make_range(min_x, max_x, min_y, max_y, min_z, max_z, blocks_per_dim,
+                          blocks_per_dim, blocks_per_dim, out);
+}
+
+int nsfps_range_get_info(const nsfps_range *r, nsfps_range_info *info) {
+  clear_error();
+  if (!r || !info) return set_error(NSFPS_ERR_ARG, "NULL argument");
+  return range_info(*r, info);
+}
+
+int nsfps_range_get_lut(const nsfps_range *r, int axis, uint32_t *lut, uint64_t cap,
+                        uint64_t *len) {
+  clear_error();
+  if (!r || !len || axis < 0 || axis > 2) return set_error(NSFPS_ERR_ARG, "bad argument");
+  RangeDev d;
+  int rc = range_to_dev(*r, &d, nullptr);
+  if (rc) return rc;
+  const uint64_t cnt = 1ull << d.bits[axis];
+  *len = cnt;
+  if (lut)
+    for (uint64_t v = 0; v < cnt && v < cap; ++v)
+      lut[v] = spread((uint32_t)v, d.bits[axis], d.pos[axis]);
+  return NSFPS_OK;
+}
+
+int nsfps_compute_bbox(const float *xyz, uint64_t n, uint32_t x_blocks, uint32_t y_blocks,
+                       uint32_t z_blocks, nsfps_range *out) {
+  clear_error();
+  if (!out) return set_error(NSFPS_ERR_ARG, "out is NULL");
+  int rc = check_points(xyz, n);
+  if (rc) return rc;
+  *out = bbox_of(xyz, n, x_blocks, y_blocks, z_blocks);
+  return NSFPS_OK;
+}
+
+int nsfps_fps_batched(const float *const *clouds, const uint64_t *n, uint64_t count,
+                      uint64_t k, const nsfps_range *ranges, int per_cloud_ranges,
+                      uint64_t *const *out, uint64_t *out_len, const int *devices,
+                      int ndev) {
+  clear_error();
+  if (count == 0) return NSFPS_OK;
+  if (!clouds || !n || !out || !out_len) return set_error(NSFPS_ERR_ARG, "NULL argument");
+  if (ndev < 1) return set_error(NSFPS_ERR_ARG, "ndev must be >= 1");
+  for (uint64_t i = 0; i < count; ++i) {
+    int rc = check_points(clouds[i], n[i]);
+    if (rc) return rc;
+    if (!out[i] && n[i] && k) return set_error(NSFPS_ERR_ARG, "out[%llu] is NULL",
+                                               (unsigned long long)i);
+  }
+  std::vector<nsfps_range> rs;
+  std::vector<uint32_t> rid(count, 0);
+  if (!ranges) {
+    for (uint64_t i = 0; i < count; ++i) {
+      rs.push_back(bbox_of(clouds[i], n[i], NSFPS_DEFAULT_X_BLOCKS, NSFPS_DEFAULT_Y_BLOCKS,
+                           NSFPS_DEFAULT_Z_BLOCKS));
+      rid[i] = (uint32_t)i;
+    }
+  } else if (per_cloud_ranges) {
+    rs.assign(ranges, ranges + count);
+    for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
+  } else {
+    rs.push_back(ranges[0]);
+  }
+  for (auto &r : rs) {
+    RangeDev d;
+    int rc = range_to_dev(r, &d, nullptr);
+    if (rc) return rc;
+  }
+  // An inverted range (max < min) gives a negative block size, so the
+  // reference's cube list reserve() throws on the first sampling step; reject
+  // it for every cloud that would reach that step.
+  for (uint64_t i = 0; i < count; ++i) {
+    if (trivial(n[i], k) || k < 2) continue;
+    const nsfps_range &r = rs[rid[i]];
+    if (r.max_x < r.min_x || r.max_y < r.min_y || r.max_z < r.min_z)
+      return set_error(NSFPS_ERR_ARG,
+                       "SpaceRange max must not be below min (got x [%g, %g], y [%g, %g], "
+                       "z [%g, %g])", r.min_x, r.max_x, r.min_y, r.max_y, r.min_z, r.max_z);
+  }
+  // the reference's early returns (src/yuezu_fps.cpp:678-688) need no GPU;
+  // the other clouds go whole, round-robin, to the devices (one host thread
+  // per device)
+  std::vector<std::vector<uint64_t>> share(ndev);
+  uint64_t ngpu = 0;
+  for (uint64_t i = 0; i < count; ++i) {
+    if (trivial(n[i], k)) fill_trivial(n[i], k, out[i], &out_len[i]);
+    else share[ngpu++ % ndev].push_back(i);
+  }
+  std::vector<int> rcs(ndev, NSFPS_OK);
+  std::vector<std::string> errs(ndev);
+  auto work = [&](int d) {
+    const int dev = devices ? devices[d] : d;
+    rcs[d] = batched_on_device(dev, clouds, n, share[d], k, rs, rid, out, out_len);
+    if (rcs[d]) errs[d] = g_err;
+  };
+  if (ndev == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int d = 0; d < ndev; ++d) th.emplace_back(work, d);
+    for (auto &t : th) t.join();
+  }
+  for (int d = 0; d < ndev; ++d)
+    if (rcs[d]) return set_error(rcs[d], "device %d: %s", devices ? devices[d] : d,
+                                 errs[d].c_str());
+  return NSFPS_OK;
+}
+
+int nsfps_fps(const float *xyz, uint64_t n, uint64_t k, const nsfps_range *range,
+              uint64_t *out, uint64_t *out_len, int device) {
+  clear_error();
+  if (!out_len) return set_error(NSFPS_ERR_ARG, "out_len is NULL");
+  int rc = check_points(xyz, n);
+  if (rc) return rc;
+  if (!out && n && k) return set_error(NSFPS_ERR_ARG, "out is NULL");
+  const float *clouds[1] = {xyz};
+  uint64_t *outs[1] = {out};
+  return nsfps_fps_batched(clouds, &n, 1, k, range, 0, outs, out_len, &device, 1);
+}
+
+int nsfps_fps_with_bbox(const float *xyz, uint64_t n, uint64_t k, uint32_t x_blocks,
+                        uint32_t y_blocks, uint32_t z_blocks, uint64_t *out,
+                        uint64_t *out_len, int device) {
+  clear_error();
+  int rc = check_points(xyz, n);
+  if (rc) return rc;
+  nsfps_range r = bbox_of(xyz, n, x_blocks, y_blocks, z_blocks);
+  return nsfps_fps(xyz, n, k, &r, out, out_len, device);
+}
+
+int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count,
+                     uint64_t k, const nsfps_range *ranges, int per_cloud_ranges,
+                     uint64_t *d_out, uint64_t *out_len, void *stream) {
+  clear_error();
+  if (count == 0) return NSFPS_OK;
+  if (!offsets || !ranges || !out_len || !d_out)
+    return set_error(NSFPS_ERR_ARG, "NULL argument");
+  int dev = 0;
+  NSFPS_CUDA(cudaGetDevice(&dev));
+  DeviceCtx *ctx = nullptr;
+  int rc = get_ctx(dev, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  cudaStream_t user = (cudaStream_t)stream;
+  std::vector<uint64_t> n(count);
+  for (uint64_t i = 0; i < count; ++i) {
+    if (offsets[i + 1] < offsets[i]) return set_error(NSFPS_ERR_ARG, "offsets must not decrease");
+    n[i] = offsets[i + 1] - offsets[i];
+  }
+  std::vector<nsfps_range> rs;
+  std::vector<uint32_t> rid(count, 0);
+  if (per_cloud_ranges) {
+    rs.assign(ranges, ranges + count);
+    for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
+  } else {
+    rs.push_back(ranges[0]);
+  }
+  // clouds needing no sampling loop are answered here; the others run as one job
+  bool all_gpu = true;
+  for (uint64_t i = 0; i < count; ++i) if (trivial(n[i], k)) all_gpu = false;
+  if (!all_gpu)
+    return set_error(NSFPS_ERR_UNSUPPORTED,
+                     "nsfps_fps_device needs 0 < k < n for every cloud");
+  if (offsets[0] != 0) d_xyz += 3 * offsets[0];
+  Job j;
+  rc = build_job(n.data(), count, k, rs, rid, j);
+  if (rc) return rc;
+  // all work is issued on the caller's stream
+  std::vector<uint32_t> lens;
+  rc = run_job(ctx, user, j, nullptr, nullptr, d_xyz, d_out, lens, nullptr);
+  if (rc) return rc;
+  for (uint64_t i = 0; i < count; ++i) out_len[i] = lens[i];
+  return NSFPS_OK;
+}
+
+int nsfps_set_profiling(int enable) {
+  g_profiling.store(enable ? 1 : 0);
+  return NSFPS_OK;
+}
+
+int nsfps_last_profile(nsfps_profile *out) {
+  if (!out) return set_error(NSFPS_ERR_ARG, "out is NULL");
+  *out = g_prof;
+  return NSFPS_OK;
+}
+
+}  // extern "C"

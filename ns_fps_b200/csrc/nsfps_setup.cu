@@ -1,0 +1,457 @@
+// nsfps_setup.cu -- per-call setup of the sampling engine, all on the GPU:
+//
+//   1. bin_points      : quantise every point to its cell and bucket exactly as
+//                        Point3D::compute_block_indices / compute_morton_code do
+//                        (src/yuezu_fps.cpp:170-199, :411-416); key = bucket
+//                        offset of the cloud + bucket.
+//   2. stable LSD radix sort of (key, point) -- 8-bit digits, one upsweep /
+//      scan / downsweep per digit.  Stability reproduces the reference's flat
+//      leaf order: buckets ascending, points of a bucket in input order
+//      (src/yuezu_fps.cpp:277-283, :431-438).
+//   3. gather_points   : sorted float4 (x, y, z, d0) with d0 the distance to the
+//                        cloud's first point, already min'ed against FLT_MAX
+//                        (build_multilevel_cache, :418-438), plus run starts.
+//   4. leaves          : runs of <= kLeafSize points of one bucket; per leaf the
+//                        bounding box, the first maximum of d0 and the cell(s)
+//                        whose cube membership selects the leaf.
+//   5. plan            : for candidate CTA counts per cloud (leaves dealt
+//                        round-robin to the CTAs), the largest point and leaf
+//                        counts any CTA would hold, so the host can size
+//                        shared memory.
+//
+// Everything here is O(N) memory; no array is sized by the number of buckets.
+#include <cfloat>
+
+#include "nsfps_internal.cuh"
+#include "nsfps_kernels.h"
+
+namespace nsfps {
+
+namespace {
+
+constexpr uint32_t kFull = 0xffffffffu;
+
+// ------------------------------------------------------------------ scans
+// Three-phase device-wide scans over uint32 (sum or max).  Tile = 4096.
+constexpr int kScanThreads = 512;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+template <bool MAX>
+__device__ __forceinline__ uint32_t sop(uint32_t a, uint32_t b) {
+  return MAX ? (a > b ? a : b) : a + b;
+}
+
+// Block-wide exclusive scan of one value per thread; returns the exclusive
+// prefix and writes the block total.  s_warp holds >= 32 entries.
+template <bool MAX>
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v,
+                                                    uint32_t *s_warp,
+                                                    uint32_t &total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t t = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl = sop<MAX>(incl, t);
+  }
+  uint32_t excl = __shfl_up_sync(kFull, incl, 1);
+  if (lane == 0) excl = 0;
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < nwarps ? s_warp[lane] : 0;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t t = __shfl_up_sync(kFull, wi, o);
+      if (lane >= o) wi = sop<MAX>(wi, t);
+    }
+    uint32_t we = __shfl_up_sync(kFull, wi, 1);
+    if (lane == 0) we = 0;
+    if (lane < nwarps) s_warp[lane] = we;
+    if (lane == nwarps - 1) s_warp[32] = wi;
+  }
+  __syncthreads();
+  const uint32_t res = sop<MAX>(s_warp[warp], excl);
+  total = s_warp[32];
+  __syncthreads();
+  return res;
+}
+
+template <bool MAX>
+__global__ void __launch_bounds__(kScanThreads)
+scan_reduce(const uint32_t *__restrict__ in, uint32_t n,
+            uint32_t *__restrict__ partial) {
+  __shared__ uint32_t s_warp[33];
+  const uint64_t base = (uint64_t)blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+  uint32_t acc = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j)
+    if (base + j < n) acc = sop<MAX>(acc, in[base + j]);
+  uint32_t total;
+  block_excl_scan<MAX>(acc, s_warp, total);
+  if (threadIdx.x == 0) partial[blockIdx.x] = total;
+}
+
+// Exclusive scan of the tile partials in place; partial[n] = grand total.
+template <bool MAX>
+__global__ void __launch_bounds__(1024)
+scan_partials(uint32_t *partial, uint32_t n) {
+  __shared__ uint32_t s_warp[33];
+  uint32_t carry = 0;
+  for (uint32_t base = 0; base < n; base += 1024) {
+    const uint32_t i = base + threadIdx.x;
+    const uint32_t v = i < n ? partial[i] : 0;
+    uint32_t total;
+    const uint32_t ex = block_excl_scan<MAX>(v, s_warp, total);
+    if (i < n) partial[i] = sop<MAX>(carry, ex);
+    carry = sop<MAX>(carry, total);
+  }
+  if (threadIdx.x == 0) partial[n] = carry;
+}
+
+template <bool MAX, bool INCLUSIVE>
+__global__ void __launch_bounds__(kScanThreads)
+scan_final(const uint32_t *in, uint32_t *out, uint32_t n,
+           const uint32_t *__restrict__ partial) {
+  // in and out may be the same array: every thread reads its own items
+  // before the block barrier inside block_excl_scan and writes them after.
+  __shared__ uint32_t s_warp[33];
+  const uint64_t base = (uint64_t)blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+  uint32_t v[kScanItems];
+  uint32_t acc = 0;
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    v[j] = (base + j < n) ? in[base + j] : 0;
+    acc = sop<MAX>(acc, v[j]);
+  }
+  uint32_t total;
+  uint32_t run = block_excl_scan<MAX>(acc, s_warp, total);
+  run = sop<MAX>(partial[blockIdx.x], run);
+#pragma unroll
+  for (int j = 0; j < kScanItems; ++j) {
+    const uint32_t nxt = sop<MAX>(run, v[j]);
+    if (base + j < n) out[base + j] = INCLUSIVE ? nxt : run;
+    run = nxt;
+  }
+}
+
+template <bool MAX, bool INCLUSIVE>
+void device_scan(const uint32_t *in, uint32_t *out, uint32_t n,
+                 uint32_t *partial, cudaStream_t st, uint32_t &launches) {
+  const uint32_t tiles = (n + kScanTile - 1) / kScanTile;
+  if (tiles == 0) return;
+  scan_reduce<MAX><<<tiles, kScanThreads, 0, st>>>(in, n, partial);
+  scan_partials<MAX><<<1, 1024, 0, st>>>(partial, tiles);
+  scan_final<MAX, INCLUSIVE><<<tiles, kScanThreads, 0, st>>>(in, out, n, partial);
+  launches += 3;
+}
+
+// ------------------------------------------------------------- radix sort
+constexpr int kRsThreads = 256;
+constexpr int kRsTile = 4096;  // 8 warps x 16 rounds x 32 lanes
+
+__global__ void __launch_bounds__(kRsThreads)
+radix_upsweep(const uint32_t *__restrict__ kin, uint32_t n, int shift,
+              uint32_t *__restrict__ hist, uint32_t ntiles) {
+  __shared__ uint32_t cnt[256];
+  cnt[threadIdx.x] = 0;
+  __syncthreads();
+  const uint64_t base = (uint64_t)blockIdx.x * kRsTile;
+#pragma unroll 4
+  for (int r = 0; r < kRsTile / kRsThreads; ++r) {
+    const uint64_t idx = base + r * kRsThreads + threadIdx.x;
+    if (idx < n) atomicAdd(&cnt[(kin[idx] >> shift) & 255u], 1u);
+  }
+  __syncthreads();
+  hist[(uint64_t)threadIdx.x * ntiles + blockIdx.x] = cnt[threadIdx.x];
+}
+
+// Stable scatter: warp w of a tile owns keys [w*512, w*512+512) of the tile in
+// 16 ordered rounds of 32; ranks inside a round come from __match_any_sync.
+__global__ void __launch_bounds__(kRsThreads)
+radix_downsweep(const uint32_t *__restrict__ kin,
+                const uint32_t *__restrict__ vin, uint32_t *__restrict__ kout,
+                uint32_t *__restrict__ vout, uint32_t n, int shift,
+                const uint32_t *__restrict__ hist, uint32_t ntiles) {
+  __shared__ uint32_t wcount[8][256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 8 * 256; i += kRsThreads) (&wcount[0][0])[i] = 0;
+  __syncthreads();
+  const uint64_t base = (uint64_t)blockIdx.x * kRsTile + warp * 512;
+  const uint32_t lt = (1u << lane) - 1u;
+  uint32_t key[16], val[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const uint64_t idx = base + r * 32 + lane;
+    const bool valid = idx < n;
+    key[r] = valid ? kin[idx] : 0u;
+    val[r] = valid ? vin[idx] : 0u;
+    const uint32_t d = valid ? ((key[r] >> shift) & 255u) : (256u + lane);
+    const uint32_t peers = __match_any_sync(kFull, d);
+    if (valid && (peers & lt) == 0) wcount[warp][d] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  {
+    const int d = tid;  // 256 threads == 256 digits
+    uint32_t running = hist[(uint64_t)d * ntiles + blockIdx.x];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t c = wcount[w][d];
+      wcount[w][d] = running;
+      running += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const uint64_t idx = base + r * 32 + lane;
+    const bool valid = idx < n;
+    const uint32_t d = valid ? ((key[r] >> shift) & 255u) : (256u + lane);
+    const uint32_t peers = __match_any_sync(kFull, d);
+    if (valid) {
+      const uint32_t pos = wcount[warp][d] + __popc(peers & lt);
+      kout[pos] = key[r];
+      vout[pos] = val[r];
+    }
+    __syncwarp();
+    if (valid && (peers & lt) == 0) wcount[warp][d] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------- binning
+__device__ __forceinline__ uint32_t cloud_of(const uint32_t *__restrict__ poff,
+                                             uint32_t B, uint32_t p) {
+  // largest c < B with poff[c] <= p
+  uint32_t lo = 0, hi = B;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (poff[mid] <= p) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(256)
+bin_points(const float *__restrict__ xyz, uint32_t n,
+           const uint32_t *__restrict__ poff, uint32_t B,
+           const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
+           const uint32_t *__restrict__ boff, uint32_t *__restrict__ keys,
+           uint32_t *__restrict__ vals) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t c = cloud_of(poff, B, i);
+  const RangeDev &r = ranges[rid[c]];
+  uint32_t cx, cy, cz;
+  cell_of(r, xyz[3ull * i], xyz[3ull * i + 1], xyz[3ull * i + 2], cx, cy, cz);
+  keys[i] = boff[c] + bucket_of_cell(r, cx, cy, cz);
+  vals[i] = i;
+}
+
+__global__ void __launch_bounds__(256)
+gather_points(const uint32_t *__restrict__ keys,
+              const uint32_t *__restrict__ vals, const float *__restrict__ xyz,
+              uint32_t n, const uint32_t *__restrict__ poff, uint32_t B,
+              float4 *__restrict__ pts, uint32_t *__restrict__ perm,
+              uint32_t *__restrict__ runflag) {
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const uint32_t v = vals[p];
+  const uint32_t c = cloud_of(poff, B, v);
+  const uint64_t q0 = 3ull * poff[c];
+  const float x = xyz[3ull * v], y = xyz[3ull * v + 1], z = xyz[3ull * v + 2];
+  const float d = sqdist(x, y, z, xyz[q0], xyz[q0 + 1], xyz[q0 + 2]);
+  pts[p] = make_float4(x, y, z, (d < FLT_MAX) ? d : FLT_MAX);
+  perm[p] = v;
+  runflag[p] = (p == 0 || keys[p] != keys[p - 1]) ? p : 0u;
+}
+
+__global__ void __launch_bounds__(256)
+leaf_flags(const uint32_t *__restrict__ run_start, uint32_t n,
+           uint32_t *__restrict__ flag) {
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p < n) flag[p] = ((p - run_start[p]) % kLeafSize) == 0 ? 1u : 0u;
+}
+
+__global__ void __launch_bounds__(256)
+leaf_scatter(const uint32_t *__restrict__ run_start,
+             const uint32_t *__restrict__ leafid, uint32_t n,
+             uint32_t *__restrict__ leaf_start, uint32_t *__restrict__ nleaves) {
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  const bool f = ((p - run_start[p]) % kLeafSize) == 0;
+  if (f) leaf_start[leafid[p]] = p;
+  if (p == n - 1) {
+    const uint32_t L = leafid[p] + (f ? 1u : 0u);
+    leaf_start[L] = n;
+    *nleaves = L;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+leaf_meta(const uint32_t *__restrict__ keys, const float4 *__restrict__ pts,
+          const uint32_t *__restrict__ leaf_start,
+          const uint32_t *__restrict__ nleaves,
+          const uint32_t *__restrict__ poff, uint32_t B,
+          const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
+          const uint32_t *__restrict__ boff, float4 *__restrict__ leaf_lo,
+          float4 *__restrict__ leaf_hi, float *__restrict__ leaf_md,
+          uint32_t *__restrict__ leaf_pre) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= *nleaves) return;
+  const uint32_t s = leaf_start[l], e = leaf_start[l + 1];
+  const uint32_t c = cloud_of(poff, B, s);
+  const RangeDev &r = ranges[rid[c]];
+  const uint32_t bucket = keys[s] - boff[c];
+  float lx = FLT_MAX, ly = FLT_MAX, lz = FLT_MAX;
+  float hx = -FLT_MAX, hy = -FLT_MAX, hz = -FLT_MAX;
+  float md = -1.0f;
+  uint32_t slot = 0;
+  for (uint32_t j = s; j < e; ++j) {
+    const float4 p = pts[j];
+    lx = fminf(lx, p.x); ly = fminf(ly, p.y); lz = fminf(lz, p.z);
+    hx = fmaxf(hx, p.x); hy = fmaxf(hy, p.y); hz = fmaxf(hz, p.z);
+    if (p.w > md) { md = p.w; slot = j - s; }
+  }
+  // Coordinates that are +-inf must not narrow the box below the points.
+  // (fminf/fmaxf already skip NaN; FLT_MAX sentinels only remain when every
+  // coordinate of an axis is NaN, and such leaves never change.)
+  uint32_t cell0 = 0, npre = 0;
+  if (r.direct) {
+    cell0 = pack_cell(gather_axis(r, 0, bucket), gather_axis(r, 1, bucket),
+                      gather_axis(r, 2, bucket));
+    npre = 1;
+  } else {
+    // every cell whose code is congruent to the bucket modulo total_blocks
+    const uint64_t lim = 1ull << r.total_bits;
+    for (int j = 0; j < kMaxPreimages; ++j) {
+      const uint64_t code = (uint64_t)bucket + (uint64_t)j * r.total;
+      if (code >= lim) break;
+      const uint32_t cx = gather_axis(r, 0, (uint32_t)code);
+      const uint32_t cy = gather_axis(r, 1, (uint32_t)code);
+      const uint32_t cz = gather_axis(r, 2, (uint32_t)code);
+      if (cx >= r.blocks[0] || cy >= r.blocks[1] || cz >= r.blocks[2]) continue;
+      const uint32_t pc = pack_cell(cx, cy, cz);
+      if (npre == 0) cell0 = pc;
+      else leaf_pre[(uint64_t)l * kMaxPreimages + npre - 1] = pc;
+      ++npre;
+    }
+  }
+  const uint32_t cnt = e - s;
+  leaf_lo[l] = make_float4(lx, ly, lz, __uint_as_float(cnt | (slot << 8) | (npre << 16)));
+  leaf_hi[l] = make_float4(hx, hy, hz, __uint_as_float(cell0));
+  leaf_md[l] = md;
+}
+
+__global__ void cloud_leaf_offsets(const uint32_t *__restrict__ leafid,
+                                   const uint32_t *__restrict__ poff, uint32_t B,
+                                   const uint32_t *__restrict__ nleaves,
+                                   uint32_t *__restrict__ loff) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < B) loff[c] = leafid[poff[c]];
+  if (c == 0) loff[B] = *nleaves;
+}
+
+// plan[3*i + {0,1,2}] = max points / leaves / extra preimages per CTA for the
+// i-th candidate CTA count, with the leaves of a cloud dealt round-robin to
+// its CTAs (leaf l of the cloud goes to CTA l % P).
+__global__ void plan_partition(const float4 *__restrict__ leaf_lo,
+                               const uint32_t *__restrict__ loff, uint32_t B,
+                               const uint32_t *__restrict__ cand, int ncand,
+                               uint32_t total_ctas, uint32_t *__restrict__ plan) {
+  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total_ctas;
+       t += gridDim.x * blockDim.x) {
+    // decode t -> (candidate i, cloud c, cta j)
+    uint32_t rem = t;
+    int i = 0;
+    for (; i < ncand; ++i) {
+      const uint32_t span = cand[i] * B;
+      if (rem < span) break;
+      rem -= span;
+    }
+    if (i >= ncand) continue;
+    const uint32_t P = cand[i];
+    const uint32_t c = rem / P, j = rem % P;
+    const uint32_t l0 = loff[c], l1 = loff[c + 1];
+    uint32_t pts = 0, leaves = 0, extra = 0;
+    for (uint32_t l = l0 + j; l < l1; l += P) {
+      const uint32_t w = __float_as_uint(leaf_lo[l].w);
+      const uint32_t npre = w >> 16;
+      pts += w & 0xffu;
+      extra += npre > 1 ? npre - 1 : 0;
+      ++leaves;
+    }
+    atomicMax(&plan[3 * i], pts);
+    atomicMax(&plan[3 * i + 1], leaves);
+    atomicMax(&plan[3 * i + 2], extra);
+  }
+}
+
+inline uint32_t cdiv(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
+
+}  // namespace
+
+// ------------------------------------------------------------------ driver
+cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
+  const uint32_t n = a.n;
+  const uint32_t B = a.B;
+  cudaError_t err;
+  if ((err = cudaMemsetAsync(a.scalars, 0, sizeof(uint32_t) * 8, st))) return err;
+
+  bin_points<<<cdiv(n, 256), 256, 0, st>>>(a.xyz, n, a.poff, B, a.rid, a.ranges,
+                                           a.boff, a.keys0, a.vals0);
+  launches += 1;
+
+  // radix passes cover the largest possible key (total buckets - 1)
+  int bits = 0;
+  while (bits < 32 && ((a.max_key >> bits) != 0)) ++bits;
+  const int passes = (bits + 7) / 8;
+
+  uint32_t *kin = a.keys0, *vin = a.vals0, *kout = a.keys1, *vout = a.vals1;
+  const uint32_t ntiles = cdiv(n, kRsTile);
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = pass * 8;
+    radix_upsweep<<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, a.hist, ntiles);
+    device_scan<false, false>(a.hist, a.hist, 256u * ntiles, a.partial, st, launches);
+    radix_downsweep<<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift,
+                                                   a.hist, ntiles);
+    launches += 2;
+    uint32_t *t;
+    t = kin; kin = kout; kout = t;
+    t = vin; vin = vout; vout = t;
+  }
+  // kin / vin now hold the sorted keys and point ids
+  gather_points<<<cdiv(n, 256), 256, 0, st>>>(kin, vin, a.xyz, n, a.poff, B, a.pts,
+                                              a.perm, a.tmp0);
+  launches += 1;
+  device_scan<true, true>(a.tmp0, a.tmp0, n, a.partial, st, launches);  // run starts
+  leaf_flags<<<cdiv(n, 256), 256, 0, st>>>(a.tmp0, n, a.tmp1);
+  launches += 1;
+  device_scan<false, false>(a.tmp1, a.tmp1, n, a.partial, st, launches);  // leaf ids
+  leaf_scatter<<<cdiv(n, 256), 256, 0, st>>>(a.tmp0, a.tmp1, n, a.leaf_start,
+                                             a.scalars + kScalarLeaves);
+  leaf_meta<<<cdiv(n, 256), 256, 0, st>>>(kin, a.pts, a.leaf_start,
+                                          a.scalars + kScalarLeaves, a.poff, B,
+                                          a.rid, a.ranges, a.boff, a.leaf_lo,
+                                          a.leaf_hi, a.leaf_md, a.leaf_pre);
+  cloud_leaf_offsets<<<cdiv(B + 1, 128), 128, 0, st>>>(a.tmp1, a.poff, B,
+                                                       a.scalars + kScalarLeaves,
+                                                       a.loff);
+  launches += 3;
+
+  if ((err = cudaMemsetAsync(a.plan, 0, sizeof(uint32_t) * 3 * a.ncand, st))) return err;
+  uint64_t total = 0;
+  for (int i = 0; i < a.ncand; ++i) total += (uint64_t)a.cand_host[i] * B;
+  if (total) {
+    const uint32_t blocks = (uint32_t)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    plan_partition<<<blocks, 256, 0, st>>>(a.leaf_lo, a.loff, B, a.cand, a.ncand,
+                                           (uint32_t)total, a.plan);
+    launches += 1;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace nsfps

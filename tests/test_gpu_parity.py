@@ -1,0 +1,169 @@
+"""GPU parity: the engine, called through its C ABI (libnsfps.so), returns
+exactly the reference's sample indices.
+
+Integer index work -> the bar is bit-exact equality (same indices, same order,
+same early stop), against
+  * golden vectors produced by the reference itself (tests/golden/), and
+  * the CPU oracle (our restatement, pinned to those goldens) on seeded
+    random clouds of many shapes.
+"""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from tests import capi
+from tests.golden import cases as C
+
+pytestmark = pytest.mark.gpu
+
+GOLD_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+GOLD = json.load(open(os.path.join(GOLD_DIR, "golden.json")))
+GOLD_NPZ = np.load(os.path.join(GOLD_DIR, "golden.npz"))
+CASES = C.by_name(include_large=True)
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def _points(name):
+    case = CASES[name]
+    if GOLD[name]["stored"] and (name + "/points") in GOLD_NPZ.files:
+        pts = GOLD_NPZ[name + "/points"]
+    else:
+        pts = case.points()
+    assert _sha(pts) == GOLD[name]["input_sha256"], f"input drift for {name}"
+    return pts
+
+
+def _check_gold(name, idx):
+    g = GOLD[name]
+    assert len(idx) == g["len"], f"{name}: length {len(idx)} != {g['len']}"
+    exp = GOLD_NPZ[name + "/indices"].astype(np.uint64)
+    got = np.asarray(idx, dtype=np.uint64)
+    if g["stored"] == "full":
+        mism = np.nonzero(got != exp)[0]
+        assert mism.size == 0, f"{name}: first mismatch at {mism[:5]}: {got[mism[:5]]} vs {exp[mism[:5]]}"
+    else:
+        assert np.array_equal(got[: len(exp)], exp), f"{name}: head differs"
+        assert _sha(got) == g["indices_sha256"], f"{name}: sequence hash differs"
+
+
+SMALL = [n for n, c in CASES.items() if not c.large]
+
+
+@pytest.mark.parametrize("name", SMALL)
+def test_golden_case(name):
+    case = CASES[name]
+    pts = _points(name)
+    idx = capi.fps(pts, case.k, case.bounds, case.blocks)
+    _check_gold(name, idx)
+
+
+def test_golden_c4_large_cloud():
+    name = "cfg_c4"
+    case = CASES[name]
+    idx = capi.fps(_points(name), case.k, case.bounds, case.blocks)
+    _check_gold(name, idx)
+
+
+def test_module_matches_capi(yf):
+    case = CASES["cfg_c1"]
+    pts = _points("cfg_c1")
+    r = yf.make_range(*case.bounds, *case.blocks)
+    a = yf.fps(pts, case.k, r)
+    assert a.dtype == np.uint64
+    _check_gold("cfg_c1", a)
+    # range=None -> compute_bbox 16^3, fps_with_bbox -> compute_bbox(xb, yb, zb)
+    b = yf.fps(pts, 300)
+    assert np.array_equal(b, oracle.fps(pts, 300, oracle.bbox(pts), (16, 16, 16)))
+    c = yf.fps_with_bbox(pts, 300, 8, 4, 2)
+    assert np.array_equal(c, oracle.fps(pts, 300, oracle.bbox(pts), (8, 4, 2)))
+    d = yf.fps(pts, n_samples=300, range={"min_x": -4, "max_x": 4, "min_y": -4, "max_y": 4,
+                                          "min_z": -4, "max_z": 4})
+    assert np.array_equal(d, oracle.fps(pts, 300, (-4, 4, -4, 4, -4, 4), (16, 16, 16)))
+
+
+def test_c3_batch_matches_oracle():
+    cfg = C.S.CONFIGS["c3"]
+    clouds = C.S.make("c3", seed=11, count=8)
+    got = capi.fps_batched(clouds, cfg.k, cfg.rng, cfg.blocks)
+    for i, cl in enumerate(clouds):
+        exp = oracle.fps(cl, cfg.k, cfg.rng, cfg.blocks)
+        assert np.array_equal(got[i], exp), f"cloud {i}"
+
+
+def test_batch_mixed_sizes_and_ranges():
+    rs = np.random.RandomState(5)
+    clouds, bounds, blocks = [], [], []
+    for i in range(9):
+        n = int(rs.choice([3, 50, 700, 5000, 20000]))
+        pts = (rs.randn(n, 3) * rs.uniform(0.5, 20, 3)).astype(np.float32)
+        clouds.append(pts)
+        lo, hi = pts.min(0) - 1e-3, pts.max(0) + 1e-3
+        bounds.append((lo[0], hi[0], lo[1], hi[1], lo[2], hi[2]))
+        blocks.append(tuple(int(v) for v in rs.choice([1, 2, 4, 8, 16, 32, 5, 12], 3)))
+    k = 600
+    got = capi.fps_batched(clouds, k, bounds, blocks, per_cloud=True)
+    for i, cl in enumerate(clouds):
+        exp = oracle.fps(cl, k, bounds[i], blocks[i])
+        assert np.array_equal(got[i], exp), f"cloud {i} n={len(cl)} blocks={blocks[i]}"
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_clouds_match_oracle(seed):
+    rs = np.random.RandomState(1000 + seed)
+    n = int(rs.choice([17, 300, 4000, 30000, 90000]))
+    kind = seed % 4
+    if kind == 0:
+        pts = rs.randn(n, 3)
+    elif kind == 1:
+        pts = rs.rand(n, 3) * [100, 40, 3]
+    elif kind == 2:  # quantised coordinates: many exact ties
+        pts = np.round(rs.randn(n, 3) * 4) / 2
+    else:  # clustered
+        c = rs.randn(8, 3) * 30
+        pts = c[rs.randint(0, 8, n)] + rs.randn(n, 3)
+    pts = pts.astype(np.float32)
+    blocks = tuple(int(v) for v in rs.choice([2, 4, 8, 16, 32, 64, 3, 7, 20], 3))
+    lo, hi = pts.min(0), pts.max(0)
+    shrink = rs.uniform(0.7, 1.1)  # sometimes clip the data (clamping)
+    mid = (lo + hi) / 2
+    half = (hi - lo) / 2 * shrink + 1e-3
+    bounds = (mid[0] - half[0], mid[0] + half[0], mid[1] - half[1], mid[1] + half[1],
+              mid[2] - half[2], mid[2] + half[2])
+    k = int(min(n - 1, rs.choice([1, 2, 10, 500, 3000]))) if n > 1 else 1
+    exp = oracle.fps(pts, k, bounds, blocks)
+    got = capi.fps(pts, k, bounds, blocks)
+    assert np.array_equal(got, exp), f"n={n} k={k} blocks={blocks}"
+
+
+def test_work_counter_equals_reference_work():
+    """The kernel's count of points in the buckets the reference updates
+    equals the oracle's count (same update set every iteration)."""
+    case = CASES["cfg_c1"]
+    pts = _points("cfg_c1")
+    capi.set_profiling(True)
+    try:
+        idx = capi.fps(pts, case.k, case.bounds, case.blocks)
+        prof = capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+    exp, sum_u, _ = oracle.fps(pts, case.k, case.bounds, case.blocks, stats=True)
+    assert np.array_equal(idx, exp)
+    assert prof.ref_points_updated == sum_u
+    assert prof.points_evaluated <= prof.ref_points_updated
+    assert prof.launches > 0 and prof.loop_ms > 0
+
+
+def test_repeated_calls_are_deterministic():
+    pts = _points("cfg_c3_cloud0")
+    case = CASES["cfg_c3_cloud0"]
+    a = capi.fps(pts, case.k, case.bounds, case.blocks)
+    b = capi.fps(pts, case.k, case.bounds, case.blocks)
+    assert np.array_equal(a, b)
+    _check_gold("cfg_c3_cloud0", a)
