@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -33,6 +34,9 @@ namespace {
 thread_local std::string g_err;
 thread_local nsfps_profile g_prof;
 std::atomic<int> g_profiling{0};
+// NSFPS_STEP_LOOP=1 in the environment selects the per-step loop even for
+// direct ranges (both loops return identical samples).
+std::atomic<int> g_force_steps{-1};
 }  // namespace
 
 int set_error(int code, const char *fmt, ...) {
@@ -205,7 +209,14 @@ constexpr int kMaxDevices = 64;
 DeviceCtx g_ctx[kMaxDevices];
 std::mutex g_ctx_mu;
 
+void read_env_once() {
+  int expected = -1;
+  const char *v = std::getenv("NSFPS_STEP_LOOP");
+  g_force_steps.compare_exchange_strong(expected, (v && v[0] == '1') ? 1 : 0);
+}
+
 int get_ctx(int device, DeviceCtx **out) {
+  read_env_once();
   int count = 0;
   cudaError_t e = cudaGetDeviceCount(&count);
   if (e != cudaSuccess || count == 0)
@@ -455,11 +466,16 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
       max_tab = std::max(max_tab, r.blocks[0] + r.blocks[1] + r.blocks[2] - 3);
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+  // direct ranges use the round-based loop, hashed ranges the per-step one
+  const bool rounds = !j.any_hashed && !g_force_steps.load();
   auto fits = [&](int i, int &m, size_t &bytes) {
     const uint32_t pts = hplan[3 * i], leaves = hplan[3 * i + 1], extra = hplan[3 * i + 2];
-    bytes = loop_smem_bytes(pts, leaves, extra, max_tab);
+    const uint32_t P = kClusterCand[i];
+    bytes = rounds ? rounds_smem_bytes(pts, leaves, max_tab)
+                   : loop_smem_bytes(pts, leaves, extra, max_tab);
+    const int cap = rounds ? rounds_max_smem(P) : max_smem;
     m = loop_leaves_per_thread(leaves);
-    return m > 0 && bytes <= (size_t)max_smem && pts <= 65535;
+    return m > 0 && bytes <= (size_t)cap && pts <= 65535;
   };
   int pi = -1, m_sel = 0;
   size_t bytes_sel = 0;
@@ -481,6 +497,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
                      max_smem);
   LoopPlan plan{};
   plan.mode = 0;
+  plan.rounds = rounds ? 1 : 0;
   plan.P = kClusterCand[pi];
   plan.leaves_per_thread = m_sel;
   plan.direct = !j.any_hashed;
@@ -511,7 +528,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   la.stats = b.stats;
   la.timeout_ns = 2000000000ll;
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[2], st));
-  NSFPS_CUDA(run_loop(la, plan, st, launches));
+  NSFPS_CUDA(plan.rounds ? run_rounds(la, plan, st, launches) : run_loop(la, plan, st, launches));
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[3], st));
   uint64_t *d_out = own_out ? b.out : d_out_user;
   NSFPS_CUDA(run_epilogue(b.out_rank, b.out_count, b.perm, b.poff, j.B, j.k, d_out, st,

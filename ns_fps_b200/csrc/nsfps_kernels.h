@@ -22,8 +22,12 @@ constexpr uint32_t kStatusBadPlan = 2u;
 constexpr int kMaxCand = 8;
 
 // Threads per CTA of the sampling loop; a thread owns up to 8 leaves
-// (template instances 1, 2, 3, 4, 6, 8).
-constexpr int kLoopThreads = 256;
+// (template instances 1, 2, 3, 4, 6, 8).  Must be a multiple of 32, at most
+// 512 (a build-time choice: -DNSFPS_LOOP_THREADS=...).
+#ifndef NSFPS_LOOP_THREADS
+#define NSFPS_LOOP_THREADS 256
+#endif
+constexpr int kLoopThreads = NSFPS_LOOP_THREADS;
 
 struct SetupArgs {
   uint32_t n;                 // points over all clouds
@@ -82,6 +86,7 @@ struct LoopArgs {
 // Which shared-memory-resident sampling kernel to run.
 struct LoopPlan {
   int mode;          // 0 = thread-block cluster (P <= 16), 1 = grid-wide
+  int rounds;        // 1 = exchange rounds of candidates (nsfps_rounds.cu)
   uint32_t P;
   int leaves_per_thread;  // template instance (1, 2, 3, 4, 6, 8)
   bool direct;            // every cloud's buckets are its cells
@@ -91,6 +96,14 @@ struct LoopPlan {
 // Smallest template instance of leaves per thread covering `leaves` leaves
 // per CTA, or 0 when none does.
 int loop_leaves_per_thread(uint32_t leaves);
+
+// The round-based loop (direct ranges only): candidates per CTA, shared
+// memory, launch.
+int rounds_candidates_per_cta(uint32_t P);
+size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab);
+int rounds_max_smem(uint32_t P);
+cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
+                       uint32_t &launches);
 
 cudaError_t run_loop(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                      uint32_t &launches);

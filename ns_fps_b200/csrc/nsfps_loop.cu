@@ -1,10 +1,11 @@
 // nsfps_loop.cu -- the persistent farthest-point-sampling kernel.
 //
 // Data placement.  The leaves of a cloud (runs of <= 16 sorted points of one
-// bucket) are dealt round-robin to its P CTAs (leaf l -> CTA l % P) and, in a
-// CTA, round-robin to its 8 warps and then to the lanes, so the leaves of one
-// cell -- which are consecutive -- land on different agents and a step's work
-// spreads over all of them.  A CTA keeps, for the whole sampling loop, its
+// bucket) are dealt round-robin to its P CTAs (leaf l -> CTA l % P), so the
+// leaves of one cell -- which are consecutive -- land on different CTAs and a
+// step's work spreads over them; inside a CTA, warp w's slot m holds 32
+// consecutive local leaves (a compact region), so one cell-box test per slot
+// skips most of a warp's leaves.  A CTA keeps, for the whole sampling loop, its
 // leaves' points in shared memory as float4 (x, y, z, current min distance)
 // and each leaf's (local start, count); every thread keeps in registers, per
 // owned leaf (up to M), the cell, bounding box, count, current maximum
@@ -51,155 +52,18 @@
 // bit; since every warp waits on the same phase, all of them give up.
 #include <cfloat>
 
-#include "nsfps_internal.cuh"
-#include "nsfps_kernels.h"
+#include "nsfps_device.cuh"
 
 namespace nsfps {
 
 namespace {
 
-constexpr uint32_t kFull = 0xffffffffu;
-constexpr int kMaxClusterP = 16;
 constexpr int kWarpsPerCta = kLoopThreads / 32;
 constexpr int kMaxAgents = kMaxClusterP * kWarpsPerCta;  // 128
-constexpr int kBufs = 4;
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile(
-      "barrier.cluster.arrive.release.aligned;\n\t"
-      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(addr), "r"(count)
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Arms the current phase of a local mbarrier: one arrival plus `bytes` of
-// expected transactions.
-__device__ __forceinline__ void mbar_arm(uint32_t addr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(addr),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-// 16 bytes into a (possibly remote) CTA's shared memory; the write counts
-// 16 transaction bytes on that CTA's mbarrier.
-__device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t mbar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
-      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(mbar)
-      : "memory");
-}
-
-__device__ __forceinline__ float sqrt_approx(float x) {
-  float r;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-// Order key of a distance: larger distance -> larger key; "no candidate"
-// (negative distance) -> 0.  Distances are never NaN (they start at FLT_MAX
-// and only take values d < old).
-__device__ __forceinline__ uint32_t dkey(float d) {
-  return d < 0.0f ? 0u : __float_as_uint(d) + 1u;
-}
-
-// A cube axis packed as lo | (width << 16); a cell index x is inside iff
-// (x - lo) <= width in unsigned arithmetic.  kNoCell packs lo = 0xffff,
-// width = 0, which no index can satisfy.
-constexpr uint32_t kNoCell = 0x0000ffffu;
-
-__device__ __forceinline__ bool in_box(uint32_t cell, uint32_t c0, uint32_t c1,
-                                       uint32_t c2) {
-  const uint32_t x = cell & 1023u, y = (cell >> 10) & 1023u, z = cell >> 20;
-  return (x - (c0 & 0xffffu)) <= (c0 >> 16) && (y - (c1 & 0xffffu)) <= (c1 >> 16) &&
-         (z - (c2 & 0xffffu)) <= (c2 >> 16);
-}
-
-// The per-axis range fields the publishing path needs, kept in registers.
-struct AxisK {
-  float mn, hi, inv, ovf, bsz;
-  int blocks;
-  const float *tab;  // shared-memory thresholds of this axis
-};
-
-// get_morton_codes_in_range (src/yuezu_fps.cpp:560-597) as a box of cells
-// around q: half-width n = (int)ceil(sqrt(D) / block_size), clipped to the
-// grid; `empty` when the reference's loops visit no cell (n < 0, or an int
-// conversion that x86 turns into INT_MIN).
-//
-// fast: n is read from the host's exact thresholds.  The guess
-// ceil(sqrt_approx(D) * inv_bs) is within one of the IEEE result: both ratios
-// agree to a few parts in 10^7, and only n < blocks - 1 matters (larger
-// half-widths all cover the whole axis), so an integer can lie between them
-// only when the exact ratio is within ~4e-4 of it.  The guess is verified
-// against tab[n-1] < D <= tab[n] (two independent loads) and moved by one
-// step; a second verification failure, which the bound excludes, would fall
-// back to walking the table.
-__device__ __forceinline__ uint32_t cube_axis(const AxisK &k, bool fast, float p,
-                                              float D, float rad_fast,
-                                              float rad_ieee, bool &empty) {
-  const uint32_t c = cell_axis(p, k.mn, k.hi, k.inv, (uint32_t)k.blocks);
-  const int top = k.blocks - 1;
-  int n;
-  if (fast) {
-    empty = empty || (D > k.ovf);
-    const float guess = fminf(ceilf(rad_fast * k.inv), (float)top);
-    n = guess > 0.0f ? (int)guess : 0;  // NaN -> 0
-    const float below = n > 0 ? k.tab[n - 1] : -1.0f;
-    const float above = n < top ? k.tab[n] : FLT_MAX;
-    if (D <= below) {
-      --n;
-      while (n > 0 && D <= k.tab[n - 1]) --n;
-    } else if (D > above) {
-      ++n;
-      while (n < top && D > k.tab[n]) ++n;
-    }
-  } else {
-    n = cvt_i32_x86(ceilf(__fdiv_rn(rad_ieee, k.bsz)));
-    empty = empty || n < 0;
-    if (n > k.blocks) n = k.blocks;
-  }
-  const int l = (int)c - n > 0 ? (int)c - n : 0;
-  const int h = (int)c + n < top ? (int)c + n : top;
-  return (uint32_t)l | ((uint32_t)(h - l) << 16);
-}
-
 // A proposal: an agent's farthest point (x, y, z, dist) and, for that point
-// as the next sample, the packed cell cube and its sorted position.
+// as the next sample, the packed cell cube and its sorted position.  The
+// (distance key, position) pair is also written to a compact array, which
+// the winner search scans without shared-memory bank conflicts.
 struct Proposal {
   float4 q;
   uint4 c;  // cube x, cube y, cube z, global sorted position
@@ -207,41 +71,11 @@ struct Proposal {
 
 struct SharedCtl {
   Proposal slot[kBufs][kMaxAgents];
+  uint2 key[kBufs][kMaxAgents];  // (dkey(dist), global sorted position)
   unsigned long long mbar[kBufs];
   uint32_t scan[33];
 };
-
-// Exclusive block scan of one value per thread.
-template <int THREADS>
-__device__ __forceinline__ uint32_t block_excl_sum(uint32_t v, uint32_t *s,
-                                                   uint32_t &total) {
-  constexpr int W = THREADS / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += t;
-  }
-  if (lane == 31) s[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    const uint32_t x = lane < W ? s[lane] : 0u;
-    uint32_t xi = x;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(kFull, xi, o);
-      if (lane >= o) xi += t;
-    }
-    s[lane] = xi - x;
-    if (lane == 31) s[32] = xi;
-  }
-  __syncthreads();
-  const uint32_t r = s[warp] + incl - v;
-  total = s[32];
-  __syncthreads();
-  return r;
-}
+constexpr uint32_t kProposalBytes = (uint32_t)(sizeof(Proposal) + sizeof(uint2));
 
 template <int M, bool DIRECT>
 __global__ void __launch_bounds__(kLoopThreads, 1)
@@ -336,12 +170,14 @@ fps_loop_cluster(const LoopArgs a) {
   ax[1].tab = s_tab + n0;
   ax[2].tab = s_tab + n0 + n1;
 
-  // per owned leaf (local index m * 256 + lane * 8 + warp), in registers
-  uint32_t cell[M], cnt[M], gst[M], lst[M], gpos[M], lpos[M];
+  // per owned leaf (local index m * 256 + warp * 32 + lane), in registers;
+  // per warp and slot m, the box of cells of the slot's 32 leaves (sbox_lo /
+  // sbox_hi, packed like cells) lets a warp skip a slot with one test
+  uint32_t cell[M], cnt[M], gst[M], lst[M], gpos[M], lpos[M], sbox_lo[M], sbox_hi[M];
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint32_t i = (uint32_t)m * THREADS + (uint32_t)lane * W + (uint32_t)warp;
+    const uint32_t i = (uint32_t)m * THREADS + (uint32_t)warp * 32 + (uint32_t)lane;
     if (i < nl) {
       const uint32_t g = gleaf(i);
       const float4 lo = a.leaf_lo[g], hi = a.leaf_hi[g];
@@ -365,9 +201,32 @@ fps_loop_cluster(const LoopArgs a) {
       bx0[m] = by0[m] = bz0[m] = 0.0f;
       bx1[m] = by1[m] = bz1[m] = 0.0f;
     }
+    // cell box of this lane's leaf (every preimage cell for hashed ranges)
+    uint32_t x0 = 1023u, y0 = 1023u, z0 = 1023u, x1 = 0u, y1 = 0u, z1 = 0u;
+    if (i < nl) {
+      const uint32_t c0 = cell[m];
+      x0 = x1 = c0 & 1023u;
+      y0 = y1 = (c0 >> 10) & 1023u;
+      z0 = z1 = c0 >> 20;
+      if (!DIRECT) {
+        const uint32_t hw = __float_as_uint(s_hi[i].w);
+        const uint32_t npre = hw >> 24, off = hw & 0xffffffu;
+        for (uint32_t j = 0; j + 1 < npre; ++j) {
+          const uint32_t c1 = s_pre[off + j];
+          x0 = min(x0, c1 & 1023u); x1 = max(x1, c1 & 1023u);
+          y0 = min(y0, (c1 >> 10) & 1023u); y1 = max(y1, (c1 >> 10) & 1023u);
+          z0 = min(z0, c1 >> 20); z1 = max(z1, c1 >> 20);
+        }
+      }
+    }
+    x0 = __reduce_min_sync(kFull, x0); y0 = __reduce_min_sync(kFull, y0);
+    z0 = __reduce_min_sync(kFull, z0); x1 = __reduce_max_sync(kFull, x1);
+    y1 = __reduce_max_sync(kFull, y1); z1 = __reduce_max_sync(kFull, z1);
+    sbox_lo[m] = pack_cell(x0, y0, z0);
+    sbox_hi[m] = pack_cell(x1, y1, z1);
   }
 
-  const uint32_t tx_bytes = (uint32_t)sizeof(Proposal) * A;
+  const uint32_t tx_bytes = kProposalBytes * A;
   if (tid == 0) {
     for (int b = 0; b < kBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
     fence_mbar_init();
@@ -379,6 +238,7 @@ fps_loop_cluster(const LoopArgs a) {
   // cluster addresses of this agent's slot 0 and of barrier 0 in CTA `lane`
   const uint32_t agent = crank * W + warp;
   const uint32_t r_slot0 = mapa(smem_u32(&ctl.slot[0][agent]), (uint32_t)lane < P ? lane : 0);
+  const uint32_t r_key0 = mapa(smem_u32(&ctl.key[0][agent]), (uint32_t)lane < P ? lane : 0);
   const uint32_t r_mbar0 = mapa(smem_u32(&ctl.mbar[0]), (uint32_t)lane < P ? lane : 0);
 
   uint32_t u_ref = 0, u_eval = 0;
@@ -387,40 +247,59 @@ fps_loop_cluster(const LoopArgs a) {
 
   // ---- this warp's farthest point -> proposal for `step`, written into
   // slot[step % kBufs][agent] of every CTA of the cluster
+  // The proposal of the previous step, re-sent unchanged when none of the
+  // warp's leaves changed since (the common case: a step touches few leaves).
+  uint4 qv = make_uint4(0u, 0u, 0u, __float_as_uint(-1.0f));
+  uint4 cv = make_uint4(kNoCell, kNoCell, kNoCell, 0u);
+  uint32_t kmax = 0u, gmin = 0xffffffffu;
+  bool dirty = true;
   auto propose = [&](uint32_t step) {
-    float bd = -1.0f;
-    uint32_t bg = 0xffffffffu, bl = 0u;
+    if (dirty) {
+      float bd = -1.0f;
+      uint32_t bg = 0xffffffffu, bl = 0u, bc = 0u;
 #pragma unroll
-    for (int m = 0; m < M; ++m)
-      if (lmax[m] > bd || (lmax[m] == bd && gpos[m] < bg)) {
-        bd = lmax[m];
-        bg = gpos[m];
-        bl = lpos[m];
+      for (int m = 0; m < M; ++m)
+        if (lmax[m] > bd || (lmax[m] == bd && gpos[m] < bg)) {
+          bd = lmax[m];
+          bg = gpos[m];
+          bl = lpos[m];
+          bc = cell[m];
+        }
+      const uint32_t key = dkey(bd);
+      kmax = __reduce_max_sync(kFull, key);
+      gmin = __reduce_min_sync(kFull, key == kmax ? bg : 0xffffffffu);
+      qv = make_uint4(0u, 0u, 0u, __float_as_uint(-1.0f));
+      cv = make_uint4(kNoCell, kNoCell, kNoCell, gmin);
+      if (kmax != 0) {
+        const uint32_t wl = __ffs(__ballot_sync(kFull, key == kmax && bg == gmin)) - 1;
+        const float4 p = s_pts[__shfl_sync(kFull, bl, wl)];
+        uint32_t qc[3];
+        if (DIRECT) {  // the point's cell is its leaf's cell
+          const uint32_t c = __shfl_sync(kFull, bc, wl);
+          qc[0] = c & 1023u;
+          qc[1] = (c >> 10) & 1023u;
+          qc[2] = c >> 20;
+        } else {
+          qc[0] = cell_axis(p.x, ax[0].mn, ax[0].hi, ax[0].inv, (uint32_t)ax[0].blocks);
+          qc[1] = cell_axis(p.y, ax[1].mn, ax[1].hi, ax[1].inv, (uint32_t)ax[1].blocks);
+          qc[2] = cell_axis(p.z, ax[2].mn, ax[2].hi, ax[2].inv, (uint32_t)ax[2].blocks);
+        }
+        uint32_t cube[3];
+        cube_of(ax, fast, qc, p.w, cube);
+        qv = make_uint4(__float_as_uint(p.x), __float_as_uint(p.y), __float_as_uint(p.z),
+                        __float_as_uint(p.w));
+        cv = make_uint4(cube[0], cube[1], cube[2], gmin);
       }
-    const uint32_t key = dkey(bd);
-    const uint32_t kmax = __reduce_max_sync(kFull, key);
-    const uint32_t gmin = __reduce_min_sync(kFull, key == kmax ? bg : 0xffffffffu);
-    uint4 qv = make_uint4(0u, 0u, 0u, __float_as_uint(-1.0f));
-    uint4 cv = make_uint4(kNoCell, kNoCell, kNoCell, 0u);
-    if (kmax != 0) {
-      const uint32_t wl = __ffs(__ballot_sync(kFull, key == kmax && bg == gmin)) - 1;
-      const float4 p = s_pts[__shfl_sync(kFull, bl, wl)];
-      const float rad_fast = sqrt_approx(p.w);
-      const float rad_ieee = fast ? 0.0f : __fsqrt_rn(p.w);
-      bool empty = false;
-      const uint32_t cx = cube_axis(ax[0], fast, p.x, p.w, rad_fast, rad_ieee, empty);
-      const uint32_t cy = cube_axis(ax[1], fast, p.y, p.w, rad_fast, rad_ieee, empty);
-      const uint32_t cz = cube_axis(ax[2], fast, p.z, p.w, rad_fast, rad_ieee, empty);
-      qv = make_uint4(__float_as_uint(p.x), __float_as_uint(p.y), __float_as_uint(p.z),
-                      __float_as_uint(p.w));
-      cv = empty ? make_uint4(kNoCell, kNoCell, kNoCell, gmin) : make_uint4(cx, cy, cz, gmin);
+      dirty = false;
     }
     if ((uint32_t)lane < P) {
       const uint32_t b = step & (kBufs - 1);
       const uint32_t rs = r_slot0 + b * (uint32_t)sizeof(ctl.slot[0]);
+      const uint32_t rk = r_key0 + b * (uint32_t)sizeof(ctl.key[0]);
       const uint32_t rm = r_mbar0 + b * (uint32_t)sizeof(ctl.mbar[0]);
       st_async_v4(rs, qv, rm);
       st_async_v4(rs + 16, cv, rm);
+      st_async_v2(rk, kmax, gmin, rm);
     }
   };
 
@@ -437,7 +316,7 @@ fps_loop_cluster(const LoopArgs a) {
       unsigned long long deadline = 0;
       uint32_t polls = 0;
       for (;;) {
-        const bool ok = mbar_try_wait(mb, parity);
+        const bool ok = mbar_try_wait(mb, parity, 20000u);
         if (__all_sync(kFull, ok)) break;
         if ((++polls & 255u) == 0) {
           const unsigned long long now = globaltimer();
@@ -457,9 +336,8 @@ fps_loop_cluster(const LoopArgs a) {
     for (int t = 0; t < kMaxAgents / 32; ++t) {
       const uint32_t idx = (uint32_t)(lane + 32 * t);
       if (idx < A) {
-        const uint32_t kk = dkey(ctl.slot[buf][idx].q.w);
-        const uint32_t rr = ctl.slot[buf][idx].c.w;
-        if (kk > bkey || (kk == bkey && rr < brank)) { bkey = kk; brank = rr; bidx = idx; }
+        const uint2 kr = ctl.key[buf][idx];
+        if (kr.x > bkey || (kr.x == bkey && kr.y < brank)) { bkey = kr.x; brank = kr.y; bidx = idx; }
       }
     }
     const uint32_t kmax = __reduce_max_sync(kFull, bkey);
@@ -477,10 +355,18 @@ fps_loop_cluster(const LoopArgs a) {
     bool need[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
+      need[m] = false;
+      // the whole slot first: does its cell box meet the cube?  (uniform)
+      const uint32_t cxl = cb.x & 0xffffu, cyl = cb.y & 0xffffu, czl = cb.z & 0xffffu;
+      const uint32_t cxh = cxl + (cb.x >> 16), cyh = cyl + (cb.y >> 16), czh = czl + (cb.z >> 16);
+      const uint32_t sl = sbox_lo[m], sh = sbox_hi[m];
+      if (cxl > (sh & 1023u) || (sl & 1023u) > cxh || cyl > ((sh >> 10) & 1023u) ||
+          ((sl >> 10) & 1023u) > cyh || czl > (sh >> 20) || (sl >> 20) > czh)
+        continue;
       bool hit = in_box(cell[m], cb.x, cb.y, cb.z);
       if (!DIRECT && !hit && cnt[m]) {
         const uint32_t hw =
-            __float_as_uint(s_hi[(uint32_t)m * THREADS + (uint32_t)lane * W + (uint32_t)warp].w);
+            __float_as_uint(s_hi[(uint32_t)m * THREADS + (uint32_t)warp * 32 + (uint32_t)lane].w);
         const uint32_t npre = hw >> 24, off = hw & 0xffffffu;
         for (uint32_t j = 0; j + 1 < npre; ++j)
           hit = hit || in_box(s_pre[off + j], cb.x, cb.y, cb.z);
@@ -498,10 +384,12 @@ fps_loop_cluster(const LoopArgs a) {
       u_eval += need[m] ? cnt[m] : 0u;
     }
     // ---- (b) the warp updates the selected leaves together, two at a time:
-    // half-warp h takes one leaf, lane j of the half its point j
+    // half-warp h takes one leaf, lane j of the half its point j; each half's
+    // new maximum is a redux over its lanes, its first position a ballot
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       uint32_t mask = __ballot_sync(kFull, need[m]);
+      dirty = dirty || mask != 0u;
       while (mask) {
         const int la = __ffs(mask) - 1;
         mask &= mask - 1;
@@ -511,33 +399,34 @@ fps_loop_cluster(const LoopArgs a) {
           mask &= mask - 1;
         }
         const int src = half ? lb2 : la;
-        float nd = -1.0f;
-        uint32_t nr = 0xffffffffu;
+        uint32_t key = 0u;  // dkey of the point's new distance; 0 = no point
         if (src >= 0) {
-          const uint32_t l = (uint32_t)m * THREADS + (uint32_t)src * W + (uint32_t)warp;
+          const uint32_t l = (uint32_t)m * THREADS + (uint32_t)warp * 32 + (uint32_t)src;
           const uint32_t lw = __float_as_uint(s_lo[l].w);
           const uint32_t start = lw & 0xffffu, c = lw >> 16;
           if ((uint32_t)j16 < c) {
             float4 p = s_pts[start + j16];
             const float d = sqdist(p.x, p.y, p.z, q.x, q.y, q.z);
             if (d < p.w) { p.w = d; s_pts[start + j16].w = d; }
-            nd = p.w;
-            nr = start + j16;
+            key = dkey(p.w);
           }
         }
-        // first maximum inside each half (positions increase with j)
-#pragma unroll
-        for (int o = 8; o; o >>= 1) {
-          const float od = __shfl_xor_sync(kFull, nd, o);
-          const uint32_t orr = __shfl_xor_sync(kFull, nr, o);
-          if (od > nd || (od == nd && orr < nr)) { nd = od; nr = orr; }
+        const uint32_t kA = __reduce_max_sync(kFull, half ? 0u : key);
+        const uint32_t kB = __reduce_max_sync(kFull, half ? key : 0u);
+        const uint32_t fA = __ffs(__ballot_sync(kFull, !half && key == kA)) - 1;
+        const uint32_t fB = __ffs(__ballot_sync(kFull, half && key == kB)) - 17;
+        // first slot holding the maximum; a leaf's points are consecutive
+        // both in shared memory and in the sorted order
+        if (lane == la) {
+          lmax[m] = __uint_as_float(kA - 1u);
+          lpos[m] = lst[m] + fA;
+          gpos[m] = gst[m] + fA;
         }
-        const float ndA = __shfl_sync(kFull, nd, 0), ndB = __shfl_sync(kFull, nd, 16);
-        const uint32_t nrA = __shfl_sync(kFull, nr, 0), nrB = __shfl_sync(kFull, nr, 16);
-        // nr is the shared-memory index; a leaf's points are consecutive both
-        // there and in the sorted order
-        if (lane == la) { lmax[m] = ndA; lpos[m] = nrA; gpos[m] = gst[m] + (nrA - lst[m]); }
-        if (lane == lb2) { lmax[m] = ndB; lpos[m] = nrB; gpos[m] = gst[m] + (nrB - lst[m]); }
+        if (lane == lb2) {
+          lmax[m] = __uint_as_float(kB - 1u);
+          lpos[m] = lst[m] + fB;
+          gpos[m] = gst[m] + fB;
+        }
       }
     }
     len = it + 1;
