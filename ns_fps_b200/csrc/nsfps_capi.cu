@@ -474,7 +474,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     bytes = rounds ? rounds_smem_bytes(pts, leaves, max_tab)
                    : loop_smem_bytes(pts, leaves, extra, max_tab);
     const int cap = rounds ? rounds_max_smem(P) : max_smem;
-    m = loop_leaves_per_thread(leaves);
+    m = rounds ? rounds_leaves_per_thread(leaves) : loop_leaves_per_thread(leaves);
     return m > 0 && bytes <= (size_t)cap && pts <= 65535;
   };
   int pi = -1, m_sel = 0;

@@ -89,6 +89,17 @@ __device__ __forceinline__ void st_async_v2(uint32_t addr, uint32_t x, uint32_t 
       : "memory");
 }
 
+// Release store / acquire load of a shared-memory word, block scope.
+__device__ __forceinline__ void st_release_cta(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ float sqrt_approx(float x) {
   float r;
   asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));

@@ -100,6 +100,7 @@ int loop_leaves_per_thread(uint32_t leaves);
 // The round-based loop (direct ranges only): candidates per CTA, shared
 // memory, launch.
 int rounds_candidates_per_cta(uint32_t P);
+int rounds_leaves_per_thread(uint32_t leaves);
 size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab);
 int rounds_max_smem(uint32_t P);
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,

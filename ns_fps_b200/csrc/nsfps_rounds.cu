@@ -32,7 +32,9 @@
 //      for all P lists;
 //   3. warp 0 replays steps on the candidates, queueing each decided sample
 //      (point, distance, cube, position) in shared memory;
-//   4. all warps apply the queued samples to their leaves, in order.
+//   4. at the same time the worker warps (1..7, which own all the leaves)
+//      apply the queued samples to their leaves, in order, as they appear
+//      (release/acquire on a shared counter).
 //
 // Buffers rotate over four rounds (a CTA publishes round r+1 only after it
 // has every round-r list), waits are bounded by %globaltimer.
@@ -43,6 +45,7 @@ namespace nsfps {
 namespace {
 
 constexpr int kWarps = kLoopThreads / 32;
+constexpr int kWorkers = kLoopThreads - 32;    // warps 1.. own the leaves
 constexpr int kMaxCands = 256;                 // P * T
 constexpr int kCandPerLane = kMaxCands / 32;   // 8
 constexpr int kQueue = 512;                    // samples decided per round, at most
@@ -66,7 +69,9 @@ struct RoundCtl {
   uint32_t wleaf[kWarps][T + 1];
   uint32_t mleaf[T + 1];                    // the CTA's T+1 best leaves
   uint32_t scan[33];
-  uint32_t nsamples;
+  uint32_t produced;  // samples of this round queued so far (release/acquire)
+  uint32_t done;      // the round's last sample is queued
+  uint32_t first;     // sample index of the round's first sample
   uint32_t finished;
 };
 
@@ -111,7 +116,7 @@ fps_rounds_cluster(const LoopArgs a) {
   const bool fast = Rg.fast_cube != 0;
   const uint32_t l0 = a.loff[cloud], l1 = a.loff[cloud + 1];
   uint32_t nl = (l1 - l0 > crank) ? (l1 - l0 - crank + P - 1) / P : 0u;
-  bool bad = nl > a.max_leaves || nl > (uint32_t)(M * THREADS) ||
+  bool bad = nl > a.max_leaves || nl > (uint32_t)(M * kWorkers) ||
              (fast && n0 + n1 + n2 > a.max_tab) || NC > (uint32_t)kMaxCands;
   if (bad) nl = 0;
   auto gleaf = [&](uint32_t i) { return l0 + crank + P * i; };
@@ -168,13 +173,14 @@ fps_rounds_cluster(const LoopArgs a) {
   ax[1].tab = s_tab + n0;
   ax[2].tab = s_tab + n0 + n1;
 
-  // per owned leaf (local index m * 256 + warp * 32 + lane), in registers
+  // per owned leaf, in registers.  Warp 0 replays the steps and owns no
+  // leaf; worker warp w (1..7) owns local leaves m * 224 + (w - 1) * 32 + lane.
   uint32_t cell[M], cnt[M], gst[M], lst[M], gpos[M], lpos[M], sbox_lo[M], sbox_hi[M];
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint32_t i = (uint32_t)m * THREADS + (uint32_t)warp * 32 + (uint32_t)lane;
-    if (i < nl) {
+    const uint32_t i = (uint32_t)m * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)lane;
+    if (warp > 0 && i < nl) {
       const uint32_t g = gleaf(i);
       const float4 lo = a.leaf_lo[g], hi = a.leaf_hi[g];
       const uint32_t w = __float_as_uint(lo.w);
@@ -198,7 +204,7 @@ fps_rounds_cluster(const LoopArgs a) {
       bx1[m] = by1[m] = bz1[m] = 0.0f;
     }
     uint32_t x0 = 1023u, y0 = 1023u, z0 = 1023u, x1 = 0u, y1 = 0u, z1 = 0u;
-    if (i < nl) {
+    if (warp > 0 && i < nl) {
       x0 = x1 = cell[m] & 1023u;
       y0 = y1 = (cell[m] >> 10) & 1023u;
       z0 = z1 = cell[m] >> 20;
@@ -226,11 +232,80 @@ fps_rounds_cluster(const LoopArgs a) {
   const long long tmo = a.timeout_ns;
   const int half = lane >> 4, j16 = lane & 15;
 
+  // ---- apply queued sample s to this worker's leaves
+  auto apply = [&](uint32_t s) {
+      const float4 q = s_samp[s].q;
+    const uint4 cb = s_samp[s].c;
+    bool need[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      need[m] = false;
+      const uint32_t cxl = cb.x & 0xffffu, cyl = cb.y & 0xffffu, czl = cb.z & 0xffffu;
+      const uint32_t cxh = cxl + (cb.x >> 16), cyh = cyl + (cb.y >> 16), czh = czl + (cb.z >> 16);
+      const uint32_t sl = sbox_lo[m], sh = sbox_hi[m];
+      if (cxl > (sh & 1023u) || (sl & 1023u) > cxh || cyl > ((sh >> 10) & 1023u) ||
+          ((sl >> 10) & 1023u) > cyh || czl > (sh >> 20) || (sl >> 20) > czh)
+        continue;
+      const bool hit = in_box(cell[m], cb.x, cb.y, cb.z);
+      const float gx = q.x < bx0[m] ? __fsub_rn(bx0[m], q.x)
+                                    : (q.x > bx1[m] ? __fsub_rn(q.x, bx1[m]) : 0.0f);
+      const float gy = q.y < by0[m] ? __fsub_rn(by0[m], q.y)
+                                    : (q.y > by1[m] ? __fsub_rn(q.y, by1[m]) : 0.0f);
+      const float gz = q.z < bz0[m] ? __fsub_rn(bz0[m], q.z)
+                                    : (q.z > bz1[m] ? __fsub_rn(q.z, bz1[m]) : 0.0f);
+      const float lbd =
+          __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
+      need[m] = hit && lbd < lmax[m];
+      u_ref += hit ? cnt[m] : 0u;
+      u_eval += need[m] ? cnt[m] : 0u;
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      uint32_t mask = __ballot_sync(kFull, need[m]);
+      while (mask) {
+        const int la = __ffs(mask) - 1;
+        mask &= mask - 1;
+        int lb2 = -1;
+        if (mask) {
+          lb2 = __ffs(mask) - 1;
+          mask &= mask - 1;
+        }
+        const int src = half ? lb2 : la;
+        uint32_t key = 0u;
+        if (src >= 0) {
+          const uint32_t l = (uint32_t)m * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)src;
+          const uint32_t lw = __float_as_uint(s_lo[l].w);
+          const uint32_t start = lw & 0xffffu, c = lw >> 16;
+          if ((uint32_t)j16 < c) {
+            float4 p = s_pts[start + j16];
+            const float d = sqdist(p.x, p.y, p.z, q.x, q.y, q.z);
+            if (d < p.w) { p.w = d; s_pts[start + j16].w = d; }
+            key = dkey(p.w);
+          }
+        }
+        const uint32_t kA = __reduce_max_sync(kFull, half ? 0u : key);
+        const uint32_t kB = __reduce_max_sync(kFull, half ? key : 0u);
+        const uint32_t fA = __ffs(__ballot_sync(kFull, !half && key == kA)) - 1;
+        const uint32_t fB = __ffs(__ballot_sync(kFull, half && key == kB)) - 17;
+        if (lane == la) {
+          lmax[m] = __uint_as_float(kA - 1u);
+          lpos[m] = lst[m] + fA;
+          gpos[m] = gst[m] + fA;
+        }
+        if (lane == lb2) {
+          lmax[m] = __uint_as_float(kB - 1u);
+          lpos[m] = lst[m] + fB;
+          gpos[m] = gst[m] + fB;
+        }
+      }
+    }
+      };
+
   for (uint32_t round = 0;; ++round) {
     const uint32_t buf = round & (kBufs - 1);
 
-    // ---- 1a. each warp: its T+1 best leaves by leaf maximum
-    {
+    // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum
+    if (warp > 0) {
       uint32_t taken = 0u;
 #pragma unroll 1
       for (int t = 0; t <= T; ++t) {
@@ -247,23 +322,29 @@ fps_rounds_cluster(const LoopArgs a) {
         if (lane == who && wk != 0ull) taken |= 1u << wm;
         if (lane == 0) {
           ctl.wkey[warp][t] = wk;
-          ctl.wleaf[warp][t] = (uint32_t)wm * THREADS + (uint32_t)warp * 32 + (uint32_t)who;
+          ctl.wleaf[warp][t] = (uint32_t)wm * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)who;
         }
       }
+    } else if (lane == 0) {
+      ctl.produced = 0u;
+      ctl.done = 0u;
+      ctl.first = it;
     }
     __syncthreads();
 
-    // ---- 1b/2. warp 0: the CTA's T+1 best leaves -> T+1 best points -> list
+    // ---- 1b/2/3. warp 0: list, exchange, replay; the workers apply the
+    // samples as they are queued
     if (warp == 0) {
-      // merge the W per-warp lists (W * (T+1) entries)
-      constexpr int E = (W * (T + 1) + 31) / 32;
+      // merge the worker warps' lists ((W - 1) * (T+1) entries)
+      constexpr int NE = (W - 1) * (T + 1);
+      constexpr int E = (NE + 31) / 32;
       unsigned long long ek[E];
       uint32_t el[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         const int idx = lane + 32 * e;
-        ek[e] = idx < W * (T + 1) ? ctl.wkey[idx / (T + 1)][idx % (T + 1)] : 0ull;
-        el[e] = idx < W * (T + 1) ? ctl.wleaf[idx / (T + 1)][idx % (T + 1)] : 0u;
+        ek[e] = idx < NE ? ctl.wkey[1 + idx / (T + 1)][idx % (T + 1)] : 0ull;
+        el[e] = idx < NE ? ctl.wleaf[1 + idx / (T + 1)][idx % (T + 1)] : 0u;
       }
       uint32_t nleaf = 0;
 #pragma unroll 1
@@ -440,7 +521,7 @@ fps_rounds_cluster(const LoopArgs a) {
             sm.q = make_float4(qx, qy, qz, qd);
             sm.c = make_uint4(cube[0], cube[1], cube[2], qpos);
             s_samp[n] = sm;
-            if (crank == 0) a.out_rank[(uint64_t)cloud * a.k + it] = qpos;
+            st_release_cta(&ctl.produced, n + 1);  // the workers may apply it now
           }
 #pragma unroll
           for (int c = 0; c < kCandPerLane; ++c)
@@ -454,92 +535,48 @@ fps_rounds_cluster(const LoopArgs a) {
         if (it >= a.k) finished = true;
       }
       if (lane == 0) {
-        ctl.nsamples = n;
         ctl.finished = finished ? 1u : 0u;
+        st_release_cta(&ctl.done, 1u);
       }
     }
-    __syncthreads();
-    const uint32_t n = ctl.nsamples;
-    const bool finished = ctl.finished != 0u;
-
-    // ---- 4. every warp applies the round's samples to its leaves, in order
+ else {
+      uint32_t s = 0;
+      unsigned long long deadline = 0;
+      uint32_t polls = 0;
+      for (;;) {
+        const uint32_t p = ld_acquire_cta(&ctl.produced);
+        if (s < p) {
 #pragma unroll 1
-    for (uint32_t s = 0; s < n; ++s) {
-      const float4 q = s_samp[s].q;
-      const uint4 cb = s_samp[s].c;
-      bool need[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        need[m] = false;
-        const uint32_t cxl = cb.x & 0xffffu, cyl = cb.y & 0xffffu, czl = cb.z & 0xffffu;
-        const uint32_t cxh = cxl + (cb.x >> 16), cyh = cyl + (cb.y >> 16), czh = czl + (cb.z >> 16);
-        const uint32_t sl = sbox_lo[m], sh = sbox_hi[m];
-        if (cxl > (sh & 1023u) || (sl & 1023u) > cxh || cyl > ((sh >> 10) & 1023u) ||
-            ((sl >> 10) & 1023u) > cyh || czl > (sh >> 20) || (sl >> 20) > czh)
+          for (; s < p; ++s) apply(s);
           continue;
-        const bool hit = in_box(cell[m], cb.x, cb.y, cb.z);
-        const float gx = q.x < bx0[m] ? __fsub_rn(bx0[m], q.x)
-                                      : (q.x > bx1[m] ? __fsub_rn(q.x, bx1[m]) : 0.0f);
-        const float gy = q.y < by0[m] ? __fsub_rn(by0[m], q.y)
-                                      : (q.y > by1[m] ? __fsub_rn(q.y, by1[m]) : 0.0f);
-        const float gz = q.z < bz0[m] ? __fsub_rn(bz0[m], q.z)
-                                      : (q.z > bz1[m] ? __fsub_rn(q.z, bz1[m]) : 0.0f);
-        const float lbd =
-            __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
-        need[m] = hit && lbd < lmax[m];
-        u_ref += hit ? cnt[m] : 0u;
-        u_eval += need[m] ? cnt[m] : 0u;
-      }
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        uint32_t mask = __ballot_sync(kFull, need[m]);
-        while (mask) {
-          const int la = __ffs(mask) - 1;
-          mask &= mask - 1;
-          int lb2 = -1;
-          if (mask) {
-            lb2 = __ffs(mask) - 1;
-            mask &= mask - 1;
-          }
-          const int src = half ? lb2 : la;
-          uint32_t key = 0u;
-          if (src >= 0) {
-            const uint32_t l = (uint32_t)m * THREADS + (uint32_t)warp * 32 + (uint32_t)src;
-            const uint32_t lw = __float_as_uint(s_lo[l].w);
-            const uint32_t start = lw & 0xffffu, c = lw >> 16;
-            if ((uint32_t)j16 < c) {
-              float4 p = s_pts[start + j16];
-              const float d = sqdist(p.x, p.y, p.z, q.x, q.y, q.z);
-              if (d < p.w) { p.w = d; s_pts[start + j16].w = d; }
-              key = dkey(p.w);
-            }
-          }
-          const uint32_t kA = __reduce_max_sync(kFull, half ? 0u : key);
-          const uint32_t kB = __reduce_max_sync(kFull, half ? key : 0u);
-          const uint32_t fA = __ffs(__ballot_sync(kFull, !half && key == kA)) - 1;
-          const uint32_t fB = __ffs(__ballot_sync(kFull, half && key == kB)) - 17;
-          if (lane == la) {
-            lmax[m] = __uint_as_float(kA - 1u);
-            lpos[m] = lst[m] + fA;
-            gpos[m] = gst[m] + fA;
-          }
-          if (lane == lb2) {
-            lmax[m] = __uint_as_float(kB - 1u);
-            lpos[m] = lst[m] + fB;
-            gpos[m] = gst[m] + fB;
-          }
+        }
+        if (ld_acquire_cta(&ctl.done)) {
+          if (s >= ld_acquire_cta(&ctl.produced)) break;
+          continue;
+        }
+        __nanosleep(32);
+        if ((++polls & 1023u) == 0) {  // bounded: warp 0 itself waits with a limit
+          const unsigned long long now = globaltimer();
+          if (deadline == 0) deadline = now + 2ull * (unsigned long long)tmo;
+          if (now > deadline) { timed_out = true; break; }
         }
       }
     }
-    if (finished) break;
-    __syncthreads();  // samples applied before the next round's lists
+    __syncthreads();  // every sample of the round applied
+    if (crank == 0) {  // the round's samples, written once the round is over
+      const uint32_t nq = ctl.produced, f = ctl.first;
+      for (uint32_t s2 = tid; s2 < nq; s2 += THREADS)
+        a.out_rank[(uint64_t)cloud * a.k + f + s2] = s_samp[s2].c.w;
+      __syncthreads();  // s_samp is rewritten by the next round
+    }
+    if (ctl.finished) break;
   }
 
   // ---- epilogue
-  if (warp == 0 && lane == 0) {
+  if (lane == 0) {
     const uint32_t status = (timed_out ? kStatusTimeout : 0u) | (bad ? kStatusBadPlan : 0u);
     if (status) atomicOr(a.scalars + kScalarStatus, status);
-    if (crank == 0) a.out_count[cloud] = it;
+    if (warp == 0 && crank == 0) a.out_count[cloud] = it;
   }
   {
     unsigned long long r64 = u_ref, e64 = u_eval;
@@ -598,6 +635,13 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
 }  // namespace
 
 int rounds_candidates_per_cta(uint32_t) { return 16; }
+
+int rounds_leaves_per_thread(uint32_t leaves) {
+  static const int ms[] = {1, 2, 3, 4, 6, 8};
+  for (int m : ms)
+    if ((uint32_t)m * kWorkers >= leaves) return m;
+  return 0;
+}
 
 size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab) {
   return (size_t)pts * 16 + (size_t)leaves * 32 + (size_t)((tab + 3) & ~3u) * 4 +
