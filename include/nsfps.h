@@ -157,6 +157,38 @@ NSFPS_API int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets,
                      int per_cloud_ranges, uint64_t *d_out, uint64_t *out_len,
                      void *stream);
 
+/* Limits of nsfps_fps_device_static(): points per call, and the size of the
+ * fixed device scratch array that holds every intermediate buffer. */
+#define NSFPS_STATIC_MAX_POINTS 65536u
+#define NSFPS_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* No counterpart in the reference (which is host-only).  One device-resident
+ * cloud, sampled without allocating any device memory: for callers that
+ * cannot allocate mid-run, such as a host that has given all device memory to
+ * its own pool, or a latency-bound loop where cudaMalloc / cudaFree would
+ * synchronise the device.  Every intermediate buffer lives in one fixed
+ * scratch array of NSFPS_STATIC_SCRATCH_BYTES per device, reserved with the
+ * library's device code.
+ *   d_xyz   n x 3 floats in DEVICE memory of the current device
+ *   n       1 <= k < n <= NSFPS_STATIC_MAX_POINTS; larger n fails with
+ *           NSFPS_ERR_ARG before any device work (k >= n or k == 0 fail with
+ *           NSFPS_ERR_UNSUPPORTED, as in nsfps_fps_device)
+ *   range   HOST memory, non-NULL
+ *   d_out   DEVICE buffer of k uint64 (original indices)
+ *   out_len HOST; receives the number of samples
+ *   stream  cudaStream_t of the current device (NULL = legacy default stream)
+ * Samples are identical to nsfps_fps_device() on the same input.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress, with
+ * that device current) and creates the device's timing events; make that
+ * first call before any stream capture.  The array is shared by all calls on
+ * a device, so overlapping calls would race on it: calls take a per-device
+ * lock and return only after their work on `stream` has finished, which runs
+ * them one at a time.  Each call clears the counters that must start at zero
+ * itself (cudaMemsetAsync on `stream`). */
+NSFPS_API int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k,
+                            const nsfps_range *range, uint64_t *d_out,
+                            uint64_t *out_len, void *stream);
+
 /* Timing and work counters of the last call on this thread: stage times in
  * milliseconds measured with CUDA events on the launching stream (setup =
  * binning, sort and leaf build; loop = the persistent sampling kernel;

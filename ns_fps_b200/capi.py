@@ -136,3 +136,19 @@ def fps_device(d_xyz_ptr: int, offsets, k: int, ranges, per_cloud: bool, d_out_p
     if rc != OK:
         raise RuntimeError(f"nsfps_fps_device rc={rc}: {last_error()}")
     return [int(v) for v in lens]
+
+
+def fps_device_static(d_xyz_ptr: int, n: int, k: int, bounds, blocks, d_out_ptr: int,
+                      stream_ptr: int = 0) -> int:
+    """nsfps_fps_device_static: one cloud of n points in device memory,
+    sampled with no device allocation (fixed scratch array; n at most
+    NSFPS_STATIC_MAX_POINTS).  Returns the sample count."""
+    r = rng(bounds, blocks)
+    ln = ctypes.c_uint64(0)
+    rc = lib().nsfps_fps_device_static(ctypes.c_void_p(d_xyz_ptr), ctypes.c_uint64(int(n)),
+                                       ctypes.c_uint64(int(k)), ctypes.byref(r),
+                                       ctypes.c_void_p(d_out_ptr), ctypes.byref(ln),
+                                       ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_fps_device_static rc={rc}: {last_error()}")
+    return int(ln.value)

@@ -647,6 +647,32 @@ int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
   return NSFPS_OK;
 }
 
+// Per-device contexts whose workspace is the fixed scratch array of
+// nsfps_static.cu: set up once per device (address and events) with that
+// device current; never grown, never freed.
+DeviceCtx g_static_ctx[kMaxDevices];
+
+int get_static_ctx(int device, DeviceCtx **out) {
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(NSFPS_ERR_ARG, "device %d out of range", device);
+  DeviceCtx *c = &g_static_ctx[device];
+  std::lock_guard<std::mutex> lk(g_ctx_mu);
+  if (!c->ready) {
+    void *p = nullptr;
+    size_t bytes = 0;
+    NSFPS_CUDA(static_scratch_address(&p, &bytes));
+    if (!p || bytes < NSFPS_STATIC_SCRATCH_BYTES)
+      return set_error(NSFPS_ERR_CUDA, "static scratch array unavailable");
+    for (auto &ev : c->ev) NSFPS_CUDA(cudaEventCreate(&ev));
+    c->ws = p;
+    c->ws_bytes = bytes;
+    c->device = device;
+    c->ready = true;
+  }
+  *out = c;
+  return NSFPS_OK;
+}
+
 }  // namespace
 }  // namespace nsfps
 
@@ -857,6 +883,47 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
   rc = run_job(ctx, user, j, nullptr, nullptr, d_xyz, d_out, lens, nullptr);
   if (rc) return rc;
   for (uint64_t i = 0; i < count; ++i) out_len[i] = lens[i];
+  return NSFPS_OK;
+}
+
+int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k,
+                            const nsfps_range *range, uint64_t *d_out, uint64_t *out_len,
+                            void *stream) {
+  clear_error();
+  if (!d_xyz || !range || !d_out || !out_len) return set_error(NSFPS_ERR_ARG, "NULL argument");
+  if (n > NSFPS_STATIC_MAX_POINTS)
+    return set_error(NSFPS_ERR_ARG,
+                     "nsfps_fps_device_static: %llu points exceed NSFPS_STATIC_MAX_POINTS (%u), "
+                     "the capacity of its fixed scratch array",
+                     (unsigned long long)n, NSFPS_STATIC_MAX_POINTS);
+  if (trivial(n, k))
+    return set_error(NSFPS_ERR_UNSUPPORTED, "nsfps_fps_device_static needs 0 < k < n");
+  const nsfps_range &r = *range;
+  if (k >= 2 && (r.max_x < r.min_x || r.max_y < r.min_y || r.max_z < r.min_z))
+    return set_error(NSFPS_ERR_ARG, "SpaceRange max must not be below min");
+  int dev = 0;
+  NSFPS_CUDA(cudaGetDevice(&dev));
+  std::vector<nsfps_range> rs(1, *range);
+  std::vector<uint32_t> rid(1, 0);
+  Job j;
+  int rc = build_job(&n, 1, k, rs, rid, j);
+  if (rc) return rc;
+  Buffers b{};
+  Carver dry(nullptr);
+  const size_t need = carve(dry, j, false, false, b);
+  if (need > NSFPS_STATIC_SCRATCH_BYTES)
+    return set_error(NSFPS_ERR_UNSUPPORTED,
+                     "nsfps_fps_device_static: needs %zu bytes of scratch, the fixed array "
+                     "holds %u", need, NSFPS_STATIC_SCRATCH_BYTES);
+  DeviceCtx *ctx = nullptr;
+  rc = get_static_ctx(dev, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  // the workspace already holds `need` bytes, so run_job allocates nothing
+  std::vector<uint32_t> lens;
+  rc = run_job(ctx, (cudaStream_t)stream, j, nullptr, nullptr, d_xyz, d_out, lens, nullptr);
+  if (rc) return rc;
+  *out_len = lens[0];
   return NSFPS_OK;
 }
 

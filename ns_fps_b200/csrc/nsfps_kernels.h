@@ -118,4 +118,8 @@ cudaError_t run_epilogue(const uint32_t *out_rank, const uint32_t *out_count,
 size_t loop_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t extra, uint32_t tab);
 int loop_max_smem();  // bytes of dynamic shared memory a CTA may use
 
+// Address and size of the fixed scratch array (nsfps_static.cu) on the
+// current device.
+cudaError_t static_scratch_address(void **ptr, size_t *bytes);
+
 }  // namespace nsfps
