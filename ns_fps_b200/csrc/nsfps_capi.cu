@@ -466,8 +466,9 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
       max_tab = std::max(max_tab, r.blocks[0] + r.blocks[1] + r.blocks[2] - 3);
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
-  // direct ranges use the round-based loop, hashed ranges the per-step one
-  const bool rounds = !j.any_hashed && !g_force_steps.load();
+  // direct ranges use the round-based loop, hashed ranges the per-step one;
+  // so do parts with more leaves than the round-based loop's threads can own
+  bool rounds = !j.any_hashed && !g_force_steps.load();
   auto fits = [&](int i, int &m, size_t &bytes) {
     const uint32_t pts = hplan[3 * i], leaves = hplan[3 * i + 1], extra = hplan[3 * i + 2];
     const uint32_t P = kClusterCand[i];
@@ -479,16 +480,24 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   };
   int pi = -1, m_sel = 0;
   size_t bytes_sel = 0;
-  for (int i = 0; i < kNumCand; ++i) {
-    int m;
-    size_t bytes;
-    if (!fits(i, m, bytes)) continue;
-    if (pi < 0) {
+  auto select = [&]() {
+    pi = -1;
+    for (int i = 0; i < kNumCand; ++i) {
+      int m;
+      size_t bytes;
+      if (!fits(i, m, bytes)) continue;
+      if (pi < 0) {
+        pi = i; m_sel = m; bytes_sel = bytes;
+        continue;
+      }
+      if (m_sel == 1 || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
       pi = i; m_sel = m; bytes_sel = bytes;
-      continue;
     }
-    if (m_sel == 1 || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
-    pi = i; m_sel = m; bytes_sel = bytes;
+  };
+  select();
+  if (pi < 0 && rounds) {
+    rounds = false;
+    select();
   }
   if (pi < 0)
     return set_error(NSFPS_ERR_UNSUPPORTED,

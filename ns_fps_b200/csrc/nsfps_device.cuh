@@ -89,6 +89,31 @@ __device__ __forceinline__ void st_async_v2(uint32_t addr, uint32_t x, uint32_t 
       : "memory");
 }
 
+// `bytes` from this CTA's shared memory to a (possibly remote) CTA's, through
+// the bulk-copy engine; the copy counts its bytes on that CTA's mbarrier.
+// Both addresses and the size are multiples of 16.  The source must have been
+// made visible to the async proxy (fence_proxy_async_smem) first.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                     uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(src), "r"(bytes), "r"(mbar)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until this thread's committed bulk copies have read their sources.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Release store / acquire load of a shared-memory word, block scope.
 __device__ __forceinline__ void st_release_cta(uint32_t *p, uint32_t v) {
   asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");

@@ -44,13 +44,28 @@ namespace nsfps {
 
 namespace {
 
+// Warps 0..kReplay-1 replay the steps, each on its share of the candidates;
+// the other warps own the leaves.  A build-time choice (1, 2 or 4).
+#ifndef NSFPS_REPLAY_WARPS
+#define NSFPS_REPLAY_WARPS 2
+#endif
+constexpr int kReplay = NSFPS_REPLAY_WARPS;
 constexpr int kWarps = kLoopThreads / 32;
-constexpr int kWorkers = kLoopThreads - 32;    // warps 1.. own the leaves
-constexpr int kMaxCands = 256;                 // P * T
-constexpr int kCandPerLane = kMaxCands / 32;   // 8
+constexpr int kWorkers = kLoopThreads - 32 * kReplay;  // leaf-owning threads
+constexpr int kMaxCands = 256;                          // P * T
+constexpr int kCandPerLane = kMaxCands / (32 * kReplay);
 constexpr int kQueue = 512;                    // samples decided per round, at most
+constexpr int kBatch = 1;                      // samples a worker applies together
+// Steps decided per replay iteration, at most (see the replay loop).
+#ifndef NSFPS_SPEC_STEPS
+#define NSFPS_SPEC_STEPS 1
+#endif
+constexpr int kSpec = NSFPS_SPEC_STEPS;
+static_assert((kBatch & (kBatch - 1)) == 0, "kBatch is a power of two");
+static_assert(kReplay == 1 || kReplay == 2 || kReplay == 4, "1, 2 or 4 replay warps");
+static_assert(kWorkers >= 64, "at least two leaf-owning warps");
 
-struct Cand {
+struct __align__(16) Cand {
   float x, y, z, d;
   uint32_t pos, cell, pad0, pad1;
 };
@@ -60,15 +75,28 @@ struct Sample {
   uint4 c;   // cube x, y, z, sorted position
 };
 
+// One CTA's published list: its T farthest points and its bound.  Copied as
+// one block into every CTA of the cluster.
+template <int T>
+struct __align__(16) CtaList {
+  Cand c[T];
+  unsigned long long bound;
+  unsigned long long pad;
+};
+
 template <int T>
 struct RoundCtl {
-  Cand cand[kBufs][kMaxCands];
-  unsigned long long bound[kBufs][kMaxClusterP];
+  CtaList<T> list[kBufs][kMaxClusterP];  // received lists, by source CTA
+  CtaList<T> stage;                      // this CTA's list, copied out from here
+  Cand live[kMaxCands];                  // the round's candidates that beat B*
+  uint32_t nlive[kReplay];
   unsigned long long mbar[kBufs];
   unsigned long long wkey[kWarps][T + 1];   // per-warp best leaves
   uint32_t wleaf[kWarps][T + 1];
   uint32_t mleaf[T + 1];                    // the CTA's T+1 best leaves
+  unsigned long long xkey[2][kReplay][kSpec];  // per replay warp best keys, by parity
   uint32_t scan[33];
+  uint32_t timed_out;  // warp 0's list wait gave up (read by the other replay warps)
   uint32_t produced;  // samples of this round queued so far (release/acquire)
   uint32_t done;      // the round's last sample is queued
   uint32_t first;     // sample index of the round's first sample
@@ -91,6 +119,58 @@ __device__ __forceinline__ unsigned long long warp_max64(unsigned long long k, i
   return ((unsigned long long)mh << 32) | ml;
 }
 
+// In-register maximum of N keys (a tree; the array is overwritten).
+template <int N>
+__device__ __forceinline__ unsigned long long tree_max64(unsigned long long (&k)[N]) {
+#pragma unroll
+  for (int st = 1; st < N; st <<= 1)
+#pragma unroll
+    for (int c = 0; c + st < N; c += 2 * st) k[c] = k[c] > k[c + st] ? k[c] : k[c + st];
+  return k[0];
+}
+
+// Largest 64-bit key over the warp (no owner lane needed).
+__device__ __forceinline__ unsigned long long warp_max64_key(unsigned long long k) {
+  const uint32_t hi = (uint32_t)(k >> 32), lo = (uint32_t)k;
+  const uint32_t mh = __reduce_max_sync(kFull, hi);
+  const uint32_t ml = __reduce_max_sync(kFull, hi == mh ? lo : 0u);
+  return ((unsigned long long)mh << 32) | ml;
+}
+
+__device__ __forceinline__ unsigned long long max64(unsigned long long a, unsigned long long b) {
+  return a > b ? a : b;
+}
+
+// True when the cube (axes packed lo | width << 16) holds no cell of the box
+// [lo, hi] (packed like cells).  Empty cubes (kNoCell) miss every box.
+__device__ __forceinline__ bool cube_misses(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t lo,
+                                            uint32_t hi) {
+  const uint32_t x0 = c0 & 0xffffu, y0 = c1 & 0xffffu, z0 = c2 & 0xffffu;
+  return x0 > (hi & 1023u) || x0 + (c0 >> 16) < (lo & 1023u) ||
+         y0 > ((hi >> 10) & 1023u) || y0 + (c1 >> 16) < ((lo >> 10) & 1023u) ||
+         z0 > (hi >> 20) || z0 + (c2 >> 16) < (lo >> 20);
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Barrier of the replay warps alone (barrier 0 is __syncthreads).
+__device__ __forceinline__ void replay_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(32 * kReplay) : "memory");
+}
+
+// Replay keys: the distance key above ((0xffffff - cloud-relative sorted
+// position) << 8 | candidate slot).  Ordered like pkey() inside one cloud
+// (positions are unique, so the slot never decides), and the winner's slot
+// and position read straight out of the key.  A cloud part of one kernel has
+// fewer than 16 * 65536 points, so the position fits in 24 bits.
+__device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
+  return ((0xffffffu - rel_pos) << 8) | slot;
+}
+
 template <int M, int T>
 __global__ void __launch_bounds__(kLoopThreads, 1)
 fps_rounds_cluster(const LoopArgs a) {
@@ -108,7 +188,8 @@ fps_rounds_cluster(const LoopArgs a) {
   float4 *s_pts = smem;
   float4 *s_lo = s_pts + a.max_pts;    // (lo.xyz, start | count << 16)
   float4 *s_hi = s_lo + a.max_leaves;  // (hi.xyz, cell)
-  float *s_tab = reinterpret_cast<float *>(s_hi + a.max_leaves);
+  uint32_t *s_gst = reinterpret_cast<uint32_t *>(s_hi + a.max_leaves);  // global sorted start
+  float *s_tab = reinterpret_cast<float *>(s_gst + ((a.max_leaves + 3u) & ~3u));
   Sample *s_samp = reinterpret_cast<Sample *>(s_tab + ((a.max_tab + 3u) & ~3u));
 
   const RangeDev &Rg = a.ranges[a.rid[cloud]];
@@ -150,6 +231,7 @@ fps_rounds_cluster(const LoopArgs a) {
         for (uint32_t j = 0; j < cntl; ++j) s_pts[lstart + j] = a.pts[gs + j];
       }
       s_hi[i] = hi;  // hi.w = cell
+      s_gst[i] = a.leaf_start[g];
     }
     pts_base += tot;
   }
@@ -172,15 +254,40 @@ fps_rounds_cluster(const LoopArgs a) {
   ax[0].tab = s_tab;
   ax[1].tab = s_tab + n0;
   ax[2].tab = s_tab + n0 + n1;
+  // Axes of at most 64 thresholds are held across the replay warp's lanes
+  // (entries lane and lane + 32): the cube half-width n_a is the number of
+  // thresholds below D (they increase with n), one ballot per 32 entries.
+  const bool regtab = fast && n0 <= 64u && n1 <= 64u && n2 <= 64u;
+  const bool wide = n0 > 32u || n1 > 32u || n2 > 32u;
+  float rt[3][2];
+#pragma unroll
+  for (int d = 0; d < 3; ++d) {
+    const uint32_t top = d == 0 ? n0 : (d == 1 ? n1 : n2);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t i = (uint32_t)lane + 32u * h;
+      rt[d][h] = (regtab && i < top) ? ax[d].tab[i] : __int_as_float(0x7f800000);
+    }
+  }
 
-  // per owned leaf, in registers.  Warp 0 replays the steps and owns no
-  // leaf; worker warp w (1..7) owns local leaves m * 224 + (w - 1) * 32 + lane.
-  uint32_t cell[M], cnt[M], gst[M], lst[M], gpos[M], lpos[M], sbox_lo[M], sbox_hi[M];
+  // per owned leaf, in registers.  The replay warps own no leaf; worker warp
+  // w (kReplay..) owns the `span` consecutive local leaves from
+  // (w - kReplay) * span, a spatially compact run (the leaves are in Morton
+  // order), as slots of 32: leaf m * 32 + lane of the run is its lane's m-th.
+  constexpr uint32_t kWorkerWarps = (uint32_t)kWorkers / 32u;
+  const uint32_t span = (nl + kWorkerWarps - 1u) / kWorkerWarps;
+  const uint32_t wbase = warp >= kReplay ? (uint32_t)(warp - kReplay) * span : 0u;
+  auto owned = [&](int m, uint32_t ln) {
+    const uint32_t r = (uint32_t)m * 32u + ln;
+    return warp >= kReplay && r < span && wbase + r < nl;
+  };
+  uint32_t cell[M], cnt[M], gst[M], gpos[M], sbox_lo[M], sbox_hi[M];
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
+  uint32_t wx0 = 1023u, wy0 = 1023u, wz0 = 1023u, wx1 = 0u, wy1 = 0u, wz1 = 0u;
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint32_t i = (uint32_t)m * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)lane;
-    if (warp > 0 && i < nl) {
+    const uint32_t i = wbase + (uint32_t)m * 32u + (uint32_t)lane;
+    if (owned(m, lane)) {
       const uint32_t g = gleaf(i);
       const float4 lo = a.leaf_lo[g], hi = a.leaf_hi[g];
       const uint32_t w = __float_as_uint(lo.w);
@@ -188,23 +295,21 @@ fps_rounds_cluster(const LoopArgs a) {
       cell[m] = __float_as_uint(hi.w);
       cnt[m] = w & 0xffu;
       gst[m] = a.leaf_start[g];
-      lst[m] = __float_as_uint(s_lo[i].w) & 0xffffu;
       lmax[m] = a.leaf_md[g];
       gpos[m] = gst[m] + slot;
-      lpos[m] = lst[m] + slot;
       bx0[m] = lo.x; by0[m] = lo.y; bz0[m] = lo.z;
       bx1[m] = hi.x; by1[m] = hi.y; bz1[m] = hi.z;
     } else {
       cell[m] = 0xffffffffu;  // z field 4095: outside every cube
       cnt[m] = 0;
-      gst[m] = lst[m] = 0;
+      gst[m] = 0;
       lmax[m] = -1.0f;
-      gpos[m] = lpos[m] = 0xffffffffu;
+      gpos[m] = 0xffffffffu;
       bx0[m] = by0[m] = bz0[m] = 0.0f;
       bx1[m] = by1[m] = bz1[m] = 0.0f;
     }
     uint32_t x0 = 1023u, y0 = 1023u, z0 = 1023u, x1 = 0u, y1 = 0u, z1 = 0u;
-    if (warp > 0 && i < nl) {
+    if (owned(m, lane)) {
       x0 = x1 = cell[m] & 1023u;
       y0 = y1 = (cell[m] >> 10) & 1023u;
       z0 = z1 = cell[m] >> 20;
@@ -214,9 +319,12 @@ fps_rounds_cluster(const LoopArgs a) {
     y1 = __reduce_max_sync(kFull, y1); z1 = __reduce_max_sync(kFull, z1);
     sbox_lo[m] = pack_cell(x0, y0, z0);
     sbox_hi[m] = pack_cell(x1, y1, z1);
+    wx0 = min(wx0, x0); wy0 = min(wy0, y0); wz0 = min(wz0, z0);
+    wx1 = max(wx1, x1); wy1 = max(wy1, y1); wz1 = max(wz1, z1);
   }
+  const uint32_t wbox_lo = pack_cell(wx0, wy0, wz0), wbox_hi = pack_cell(wx1, wy1, wz1);
 
-  const uint32_t tx_bytes = P * (uint32_t)(T * sizeof(Cand) + sizeof(unsigned long long));
+  const uint32_t tx_bytes = P * (uint32_t)sizeof(CtaList<T>);
   if (tid == 0) {
     for (int b = 0; b < kBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
     fence_mbar_init();
@@ -232,36 +340,56 @@ fps_rounds_cluster(const LoopArgs a) {
   const long long tmo = a.timeout_ns;
   const int half = lane >> 4, j16 = lane & 15;
 
-  // ---- apply queued sample s to this worker's leaves
-  auto apply = [&](uint32_t s) {
-      const float4 q = s_samp[s].q;
-    const uint4 cb = s_samp[s].c;
-    bool need[M];
+  // ---- apply queued samples s0 .. s0+nb-1 (nb <= kBatch) to this worker's
+  // leaves.  Each point takes min(old, d) over the samples whose cube holds its
+  // cell -- the reference's per-step updates, whose result does not depend on
+  // their order.  A sample whose cube misses the warp's cell box, or a slot's,
+  // is skipped for all of it; a leaf is skipped for a sample when the
+  // sample's distance to the leaf box is not below the leaf maximum from
+  // before the batch (no smaller than the current one, so the skip is exact).
+  auto apply = [&](uint32_t s0, uint32_t nb) {
+    float qx[kBatch], qy[kBatch], qz[kBatch];
+    uint32_t c0[kBatch], c1[kBatch], c2[kBatch];
+    uint32_t live = 0u;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      need[m] = false;
-      const uint32_t cxl = cb.x & 0xffffu, cyl = cb.y & 0xffffu, czl = cb.z & 0xffffu;
-      const uint32_t cxh = cxl + (cb.x >> 16), cyh = cyl + (cb.y >> 16), czh = czl + (cb.z >> 16);
-      const uint32_t sl = sbox_lo[m], sh = sbox_hi[m];
-      if (cxl > (sh & 1023u) || (sl & 1023u) > cxh || cyl > ((sh >> 10) & 1023u) ||
-          ((sl >> 10) & 1023u) > cyh || czl > (sh >> 20) || (sl >> 20) > czh)
-        continue;
-      const bool hit = in_box(cell[m], cb.x, cb.y, cb.z);
-      const float gx = q.x < bx0[m] ? __fsub_rn(bx0[m], q.x)
-                                    : (q.x > bx1[m] ? __fsub_rn(q.x, bx1[m]) : 0.0f);
-      const float gy = q.y < by0[m] ? __fsub_rn(by0[m], q.y)
-                                    : (q.y > by1[m] ? __fsub_rn(q.y, by1[m]) : 0.0f);
-      const float gz = q.z < bz0[m] ? __fsub_rn(bz0[m], q.z)
-                                    : (q.z > bz1[m] ? __fsub_rn(q.z, bz1[m]) : 0.0f);
-      const float lbd =
-          __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
-      need[m] = hit && lbd < lmax[m];
-      u_ref += hit ? cnt[m] : 0u;
-      u_eval += need[m] ? cnt[m] : 0u;
+    for (int j = 0; j < kBatch; ++j) {
+      const bool on = (uint32_t)j < nb;
+      const float4 q = on ? s_samp[s0 + j].q : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const uint4 cb = on ? s_samp[s0 + j].c : make_uint4(kNoCell, kNoCell, kNoCell, 0u);
+      qx[j] = q.x; qy[j] = q.y; qz[j] = q.z;
+      c0[j] = cb.x; c1[j] = cb.y; c2[j] = cb.z;
+      live |= cube_misses(cb.x, cb.y, cb.z, wbox_lo, wbox_hi) ? 0u : (1u << j);
     }
+    if (live == 0u) return;
+    uint32_t needb[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      uint32_t mask = __ballot_sync(kFull, need[m]);
+      needb[m] = 0u;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        if (!((live >> j) & 1u) || cube_misses(c0[j], c1[j], c2[j], sbox_lo[m], sbox_hi[m]))
+          continue;
+        const bool hit = in_box(cell[m], c0[j], c1[j], c2[j]);
+        const float gx = qx[j] < bx0[m] ? __fsub_rn(bx0[m], qx[j])
+                                        : (qx[j] > bx1[m] ? __fsub_rn(qx[j], bx1[m]) : 0.0f);
+        const float gy = qy[j] < by0[m] ? __fsub_rn(by0[m], qy[j])
+                                        : (qy[j] > by1[m] ? __fsub_rn(qy[j], by1[m]) : 0.0f);
+        const float gz = qz[j] < bz0[m] ? __fsub_rn(bz0[m], qz[j])
+                                        : (qz[j] > bz1[m] ? __fsub_rn(qz[j], bz1[m]) : 0.0f);
+        const float lbd =
+            __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
+        const bool need = hit && lbd < lmax[m];
+        u_ref += hit ? cnt[m] : 0u;
+        u_eval += need ? cnt[m] : 0u;
+        needb[m] |= need ? (1u << j) : 0u;
+      }
+    }
+    uint32_t mk[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) mk[m] = __ballot_sync(kFull, needb[m] != 0u);
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      uint32_t mask = mk[m];
       while (mask) {
         const int la = __ffs(mask) - 1;
         mask &= mask - 1;
@@ -270,17 +398,25 @@ fps_rounds_cluster(const LoopArgs a) {
           lb2 = __ffs(mask) - 1;
           mask &= mask - 1;
         }
+        // half-warp h updates leaf la (h = 0) or lb2 (h = 1), a point per lane
         const int src = half ? lb2 : la;
+        const uint32_t nbits = __shfl_sync(kFull, needb[m], src < 0 ? 0 : src);
         uint32_t key = 0u;
         if (src >= 0) {
-          const uint32_t l = (uint32_t)m * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)src;
+          const uint32_t l = wbase + (uint32_t)m * 32u + (uint32_t)src;
           const uint32_t lw = __float_as_uint(s_lo[l].w);
           const uint32_t start = lw & 0xffffu, c = lw >> 16;
           if ((uint32_t)j16 < c) {
             float4 p = s_pts[start + j16];
-            const float d = sqdist(p.x, p.y, p.z, q.x, q.y, q.z);
-            if (d < p.w) { p.w = d; s_pts[start + j16].w = d; }
-            key = dkey(p.w);
+            float w = p.w;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j)
+              if ((nbits >> j) & 1u) {
+                const float d = sqdist(p.x, p.y, p.z, qx[j], qy[j], qz[j]);
+                if (d < w) w = d;
+              }
+            if (w < p.w) s_pts[start + j16].w = w;
+            key = dkey(w);
           }
         }
         const uint32_t kA = __reduce_max_sync(kFull, half ? 0u : key);
@@ -289,257 +425,386 @@ fps_rounds_cluster(const LoopArgs a) {
         const uint32_t fB = __ffs(__ballot_sync(kFull, half && key == kB)) - 17;
         if (lane == la) {
           lmax[m] = __uint_as_float(kA - 1u);
-          lpos[m] = lst[m] + fA;
           gpos[m] = gst[m] + fA;
         }
         if (lane == lb2) {
           lmax[m] = __uint_as_float(kB - 1u);
-          lpos[m] = lst[m] + fB;
           gpos[m] = gst[m] + fB;
         }
       }
     }
-      };
+  };
 
+  uint32_t out_n = 0, out_first = 0;  // the round's samples (worker warps)
   for (uint32_t round = 0;; ++round) {
     const uint32_t buf = round & (kBufs - 1);
 
-    // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum
-    if (warp > 0) {
-      uint32_t taken = 0u;
+    // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum, in
+    // order (keys are unique: every leaf has its own sorted position)
+    if (warp >= kReplay) {
+      unsigned long long lk[M];
+      int rk[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        lk[m] = pkey(lmax[m], gpos[m]);  // 0 for a leaf this lane does not own
+        rk[m] = -1;
+      }
+      if (lane <= T) ctl.wkey[warp][lane] = 0ull;
 #pragma unroll 1
       for (int t = 0; t <= T; ++t) {
-        unsigned long long best = 0ull;
-        int bm = 0;
+        unsigned long long tk[M];
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const unsigned long long k = ((taken >> m) & 1u) ? 0ull : pkey(lmax[m], gpos[m]);
-          if (k > best) { best = k; bm = m; }
-        }
-        int who;
-        const unsigned long long wk = warp_max64(best, who);
-        const int wm = __shfl_sync(kFull, bm, who);
-        if (lane == who && wk != 0ull) taken |= 1u << wm;
-        if (lane == 0) {
-          ctl.wkey[warp][t] = wk;
-          ctl.wleaf[warp][t] = (uint32_t)wm * kWorkers + (uint32_t)(warp - 1) * 32 + (uint32_t)who;
-        }
+        for (int m = 0; m < M; ++m) tk[m] = lk[m];
+        const unsigned long long wk = warp_max64_key(tree_max64(tk));
+        if (wk == 0ull) break;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          if (lk[m] == wk) { lk[m] = 0ull; rk[m] = t; }
       }
-    } else if (lane == 0) {
+      __syncwarp();
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+        if (rk[m] >= 0) {
+          ctl.wkey[warp][rk[m]] = pkey(lmax[m], gpos[m]);
+          ctl.wleaf[warp][rk[m]] = wbase + (uint32_t)m * 32u + (uint32_t)lane;
+        }
+    } else if (warp == 0 && lane == 0) {
       ctl.produced = 0u;
       ctl.done = 0u;
       ctl.first = it;
     }
     __syncthreads();
 
-    // ---- 1b/2/3. warp 0: list, exchange, replay; the workers apply the
-    // samples as they are queued
-    if (warp == 0) {
-      // merge the worker warps' lists ((W - 1) * (T+1) entries)
-      constexpr int NE = (W - 1) * (T + 1);
-      constexpr int E = (NE + 31) / 32;
-      unsigned long long ek[E];
-      uint32_t el[E];
+    // ---- 1b/2/3. warp 0: list and exchange; the replay warps: replay; the
+    // workers apply the samples as they are queued
+    if (warp < kReplay) {
+      if (warp == 0) {
+        // merge the worker warps' lists ((W - kReplay) * (T+1) entries)
+        constexpr int NE = (W - kReplay) * (T + 1);
+        constexpr int E = (NE + 31) / 32;
+        unsigned long long ek[E];
+        uint32_t el[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int idx = lane + 32 * e;
-        ek[e] = idx < NE ? ctl.wkey[1 + idx / (T + 1)][idx % (T + 1)] : 0ull;
-        el[e] = idx < NE ? ctl.wleaf[1 + idx / (T + 1)][idx % (T + 1)] : 0u;
-      }
-      uint32_t nleaf = 0;
+        for (int e = 0; e < E; ++e) {
+          const int idx = lane + 32 * e;
+          ek[e] = idx < NE ? ctl.wkey[kReplay + idx / (T + 1)][idx % (T + 1)] : 0ull;
+          el[e] = idx < NE ? ctl.wleaf[kReplay + idx / (T + 1)][idx % (T + 1)] : 0u;
+        }
+        int er[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) er[e] = -1;
+        uint32_t nleaf = 0;
 #pragma unroll 1
-      for (int t = 0; t <= T; ++t) {
-        unsigned long long best = 0ull;
-        int be = 0;
+        for (int t = 0; t <= T; ++t) {
+          unsigned long long tk[E];
 #pragma unroll
-        for (int e = 0; e < E; ++e)
-          if (ek[e] > best) { best = ek[e]; be = e; }
-        int who;
-        const unsigned long long wk = warp_max64(best, who);
-        if (wk == 0ull) break;
-        uint32_t lsel = 0u;
-#pragma unroll
-        for (int e = 0; e < E; ++e)
-          if (e == be) lsel = el[e];
-        const uint32_t wl = __shfl_sync(kFull, lsel, who);
-        if (lane == who) {
+          for (int e = 0; e < E; ++e) tk[e] = ek[e];
+          const unsigned long long wk = warp_max64_key(tree_max64(tk));
+          if (wk == 0ull) break;
 #pragma unroll
           for (int e = 0; e < E; ++e)
-            if (e == be) ek[e] = 0ull;
+            if (ek[e] == wk) { ek[e] = 0ull; er[e] = t; }
+          ++nleaf;
         }
-        if (lane == 0) ctl.mleaf[t] = wl;
-        ++nleaf;
-      }
-      __syncwarp();
-      // gather the points of those leaves; half-warp h takes leaf 2r + h
-      constexpr int G = (T + 2) / 2;  // points held per lane
-      unsigned long long gk[G];
-      float4 gp[G];
-      uint32_t gc[G];
 #pragma unroll
-      for (int r = 0; r < G; ++r) {
-        const uint32_t li = 2u * r + (uint32_t)half;
-        gk[r] = 0ull;
-        gp[r] = make_float4(0, 0, 0, -1.0f);
-        gc[r] = 0u;
-        if (li < nleaf) {
-          const uint32_t leaf = ctl.mleaf[li];
-          const uint32_t lw = __float_as_uint(s_lo[leaf].w);
-          const uint32_t start = lw & 0xffffu, c = lw >> 16;
-          if ((uint32_t)j16 < c) {
-            gp[r] = s_pts[start + j16];
-            gc[r] = __float_as_uint(s_hi[leaf].w);
-            // sorted position: the leaf's global start + slot
-            const uint32_t gstart = a.leaf_start[gleaf(leaf)];
-            gk[r] = pkey(gp[r].w, gstart + j16);
+        for (int e = 0; e < E; ++e)
+          if (er[e] >= 0) ctl.mleaf[er[e]] = el[e];
+        __syncwarp();
+        // gather the points of those leaves; half-warp h takes leaf 2r + h
+        constexpr int G = (T + 2) / 2;  // points held per lane
+        unsigned long long gk[G];
+        float4 gp[G];
+        uint32_t gc[G], gq[G];
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          const uint32_t li = 2u * r + (uint32_t)half;
+          gk[r] = 0ull;
+          gp[r] = make_float4(0, 0, 0, -1.0f);
+          gc[r] = 0u;
+          gq[r] = 0xffffffffu;
+          if (li < nleaf) {
+            const uint32_t leaf = ctl.mleaf[li];
+            const uint32_t lw = __float_as_uint(s_lo[leaf].w);
+            const uint32_t start = lw & 0xffffu, c = lw >> 16;
+            if ((uint32_t)j16 < c) {
+              gp[r] = s_pts[start + j16];
+              gc[r] = __float_as_uint(s_hi[leaf].w);
+              // sorted position: the leaf's global start + slot
+              gq[r] = s_gst[leaf] + (uint32_t)j16;
+              gk[r] = pkey(gp[r].w, gq[r]);
+            }
           }
         }
-      }
-      // the T+1 best points: the first T are the list, the next is the bound
-      unsigned long long bound = 0ull;
+        // the T+1 best points: the first T are the list, the next is the bound
+        unsigned long long bound = 0ull;
+        int gr[G];
+#pragma unroll
+        for (int r = 0; r < G; ++r) gr[r] = -1;
+        uint32_t nsel = 0;
 #pragma unroll 1
-      for (int t = 0; t <= T; ++t) {
-        unsigned long long best = 0ull;
-        int br = 0;
+        for (int t = 0; t <= T; ++t) {
+          unsigned long long tk[G];
 #pragma unroll
-        for (int r = 0; r < G; ++r)
-          if (gk[r] > best) { best = gk[r]; br = r; }
-        int who;
-        const unsigned long long wk = warp_max64(best, who);
-        if (t == T) { bound = wk; break; }
-        float4 p = make_float4(0, 0, 0, -1.0f);
-        uint32_t c = 0u;
-#pragma unroll
-        for (int r = 0; r < G; ++r)
-          if (r == br) { p = gp[r]; c = gc[r]; }
-        p.x = __shfl_sync(kFull, p.x, who);
-        p.y = __shfl_sync(kFull, p.y, who);
-        p.z = __shfl_sync(kFull, p.z, who);
-        p.w = __shfl_sync(kFull, p.w, who);
-        c = __shfl_sync(kFull, c, who);
-        if (lane == who) {
+          for (int r = 0; r < G; ++r) tk[r] = gk[r];
+          const unsigned long long wk = warp_max64_key(tree_max64(tk));
+          if (t == T) { bound = wk; break; }
+          if (wk == 0ull) break;
 #pragma unroll
           for (int r = 0; r < G; ++r)
-            if (r == br) gk[r] = 0ull;
+            if (gk[r] == wk) { gk[r] = 0ull; gr[r] = t; }
+          ++nsel;
         }
-        // candidate t of this CTA: to every CTA's cand[buf][crank * T + t]
-        Cand cd;
-        if (wk == 0ull) {
+        // stage the list (after the previous round's copies have read it),
+        // then copy it into every CTA's list[buf][crank]
+        if ((uint32_t)lane < P) bulk_wait_read_all();
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < G; ++r)
+          if (gr[r] >= 0) {
+            Cand cd;
+            cd.x = gp[r].x; cd.y = gp[r].y; cd.z = gp[r].z; cd.d = gp[r].w;
+            cd.pos = gq[r]; cd.cell = gc[r]; cd.pad0 = cd.pad1 = 0u;
+            ctl.stage.c[gr[r]] = cd;
+          }
+        if ((uint32_t)lane >= nsel && lane < T) {
+          Cand cd;
           cd.x = cd.y = cd.z = 0.0f;
           cd.d = -1.0f;
           cd.pos = 0xffffffffu;
           cd.cell = 0xffffffffu;
-        } else {
-          cd.x = p.x; cd.y = p.y; cd.z = p.z; cd.d = p.w;
-          cd.pos = 0xffffffffu - (uint32_t)wk;
-          cd.cell = c;
+          cd.pad0 = cd.pad1 = 0u;
+          ctl.stage.c[lane] = cd;
         }
+        if (lane == 0) {
+          ctl.stage.bound = bound;
+          ctl.stage.pad = 0ull;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
         if ((uint32_t)lane < P) {
-          const uint32_t ra = mapa(smem_u32(&ctl.cand[buf][crank * T + t]), lane);
+          const uint32_t ra = mapa(smem_u32(&ctl.list[buf][crank]), lane);
           const uint32_t rm = mapa(smem_u32(&ctl.mbar[buf]), lane);
-          st_async_v4(ra, make_uint4(__float_as_uint(cd.x), __float_as_uint(cd.y),
-                                     __float_as_uint(cd.z), __float_as_uint(cd.d)), rm);
-          st_async_v4(ra + 16, make_uint4(cd.pos, cd.cell, 0u, 0u), rm);
+          bulk_copy_to_cluster(ra, smem_u32(&ctl.stage), (uint32_t)sizeof(CtaList<T>), rm);
+          bulk_commit();
         }
-      }
-      if ((uint32_t)lane < P) {
-        const uint32_t ra = mapa(smem_u32(&ctl.bound[buf][crank]), lane);
-        const uint32_t rm = mapa(smem_u32(&ctl.mbar[buf]), lane);
-        st_async_v2(ra, (uint32_t)bound, (uint32_t)(bound >> 32), rm);
-      }
 
-      // ---- wait for every CTA's list (bounded)
-      const uint32_t mb = smem_u32(&ctl.mbar[buf]);
-      const uint32_t parity = (round / kBufs) & 1u;
-      unsigned long long deadline = 0;
-      uint32_t polls = 0;
-      for (;;) {
-        const bool ok = mbar_try_wait(mb, parity, 20000u);
-        if (__all_sync(kFull, ok)) break;
-        if ((++polls & 255u) == 0) {
-          const unsigned long long now = globaltimer();
-          if (deadline == 0) deadline = now + (unsigned long long)tmo;
-          if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
+        // ---- wait for every CTA's list (bounded)
+        const uint32_t mb = smem_u32(&ctl.mbar[buf]);
+        const uint32_t parity = (round / kBufs) & 1u;
+        unsigned long long deadline = 0;
+        uint32_t polls = 0;
+        for (;;) {
+          const bool ok = mbar_try_wait(mb, parity, 20000u);
+          if (__all_sync(kFull, ok)) break;
+          if ((++polls & 255u) == 0) {
+            const unsigned long long now = globaltimer();
+            if (deadline == 0) deadline = now + (unsigned long long)tmo;
+            if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
+          }
+        }
+        if (lane == 0) {
+          mbar_arm(mb, tx_bytes);  // for round + kBufs
+          ctl.timed_out = timed_out ? 1u : 0u;
         }
       }
-      if (lane == 0) mbar_arm(mb, tx_bytes);  // for round + kBufs
+      // every list is in and the timeout flag is set
+      if (kReplay > 1) replay_sync(); else __syncwarp();
 
       // ---- 3. replay steps on the candidates
       uint32_t n = 0;
-      bool finished = timed_out;
-      if (!timed_out) {
-        float cx[kCandPerLane], cy[kCandPerLane], cz[kCandPerLane], cdd[kCandPerLane];
-        uint32_t cpos[kCandPerLane], ccell[kCandPerLane];
+      bool finished = ctl.timed_out != 0u;
+      if (!finished) {
+        const uint32_t pbase = a.poff[cloud];
+        // B* = the largest bound, in the replay key's encoding
+        unsigned long long bl = 0ull;
+        if ((uint32_t)lane < P) {
+          bl = ctl.list[buf][lane].bound;
+          if (bl != 0ull)
+            bl = (bl & 0xffffffff00000000ull) |
+                 replay_lo((0xffffffffu - (uint32_t)bl) - pbase, 0u);
+        }
+        const unsigned long long bstar = warp_max64_key(bl);
+        // Only candidates that beat B* can be chosen this round (keys only
+        // decrease): compact them into ctl.live, so the steps touch no other.
+        uint32_t nl_w = 0, lslot[kCandPerLane];
+        bool lv[kCandPerLane];
 #pragma unroll
         for (int c = 0; c < kCandPerLane; ++c) {
-          const uint32_t idx = (uint32_t)(lane + 32 * c);
+          const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
+          lv[c] = false;
           if (idx < NC) {
-            const Cand cd = ctl.cand[buf][idx];
+            const Cand &cd = ctl.list[buf][idx / T].c[idx % T];
+            lv[c] = cd.d >= 0.0f &&
+                    (((unsigned long long)dkey(cd.d) << 32) | replay_lo(cd.pos - pbase, 0u)) > bstar;
+          }
+          const uint32_t bm = __ballot_sync(kFull, lv[c]);
+          lslot[c] = nl_w + __popc(bm & lanemask_lt());
+          nl_w += __popc(bm);
+        }
+        if (lane == 0) ctl.nlive[warp] = nl_w;
+        if (kReplay > 1) replay_sync(); else __syncwarp();
+        uint32_t L = 0, off = 0;
+#pragma unroll
+        for (int w = 0; w < kReplay; ++w) {
+          const uint32_t v = ctl.nlive[w];
+          off += w < warp ? v : 0u;
+          L += v;
+        }
+#pragma unroll
+        for (int c = 0; c < kCandPerLane; ++c)
+          if (lv[c]) {
+            const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
+            ctl.live[off + lslot[c]] = ctl.list[buf][idx / T].c[idx % T];
+          }
+        if (kReplay > 1) replay_sync(); else __syncwarp();
+        // live candidate i sits in lane i % 32 of warp (i / 32) % kReplay, row
+        // i / (32 * kReplay); rows past L are empty on every warp
+        float cx[kCandPerLane], cy[kCandPerLane], cz[kCandPerLane], cdd[kCandPerLane];
+        uint32_t clo[kCandPerLane], ccell[kCandPerLane];
+#pragma unroll
+        for (int c = 0; c < kCandPerLane; ++c) {
+          const uint32_t idx = (uint32_t)(32 * kReplay * c + 32 * warp + lane);
+          cx[c] = cy[c] = cz[c] = 0.0f;
+          cdd[c] = -1.0f;
+          clo[c] = 0u;  // no candidate: key 0
+          ccell[c] = 0xffffffffu;
+          if (idx < L) {
+            const Cand cd = ctl.live[idx];
             cx[c] = cd.x; cy[c] = cd.y; cz[c] = cd.z; cdd[c] = cd.d;
-            cpos[c] = cd.pos; ccell[c] = cd.cell;
-          } else {
-            cx[c] = cy[c] = cz[c] = 0.0f; cdd[c] = -1.0f;
-            cpos[c] = 0xffffffffu; ccell[c] = 0xffffffffu;
+            clo[c] = replay_lo(cd.pos - pbase, idx);
+            ccell[c] = cd.cell;
           }
         }
-        // B* = the largest bound
-        unsigned long long bl = 0ull;
-        if ((uint32_t)lane < P) bl = ctl.bound[buf][lane];
-        int who;
-        const unsigned long long bstar = warp_max64(bl, who);
+        const uint32_t rows = (L + 32u * kReplay - 1u) / (32u * kReplay);
 
+        // Each iteration takes the kSpec best candidates W0 > W1 > ... and
+        // decides the longest prefix of them that are the reference's next
+        // steps: Wj (j >= 1) is, when it beats B*, has a positive distance and
+        // lies outside the cubes of W0..Wj-1 (all non-empty).  Then none of
+        // those steps changes Wj's distance while each drops its own winner's
+        // to 0, so after them Wj is the largest key, exactly as in the
+        // reference; the candidates' updates commute (min).
+        uint32_t iter = 0;
         while (it < a.k && n < (uint32_t)kQueue) {
-          unsigned long long best = 0ull;
-          int bc = 0;
-#pragma unroll
-          for (int c = 0; c < kCandPerLane; ++c) {
-            const unsigned long long k = pkey(cdd[c], cpos[c]);
-            if (cdd[c] >= 0.0f && k > best) { best = k; bc = c; }
-          }
-          const unsigned long long wk = warp_max64(best, who);
-          if (wk <= bstar) break;  // not certain: some unlisted point may win
-          float qx = 0.0f, qy = 0.0f, qz = 0.0f, qd = 0.0f;
-          uint32_t qcell = 0u;
+          unsigned long long kk[kCandPerLane];
 #pragma unroll
           for (int c = 0; c < kCandPerLane; ++c)
-            if (c == bc) { qx = cx[c]; qy = cy[c]; qz = cz[c]; qd = cdd[c]; qcell = ccell[c]; }
-          qx = __shfl_sync(kFull, qx, who);
-          qy = __shfl_sync(kFull, qy, who);
-          qz = __shfl_sync(kFull, qz, who);
-          qd = __shfl_sync(kFull, qd, who);
-          qcell = __shfl_sync(kFull, qcell, who);
-          if (!(qd > 0.0f)) {  // src/yuezu_fps.cpp:705-706
+            kk[c] = (uint32_t)c < rows ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
+          unsigned long long wt[kSpec];  // this warp's best keys, in order
+#pragma unroll
+          for (int j = 0; j < kSpec; ++j) {
+            unsigned long long tk[kCandPerLane];
+#pragma unroll
+            for (int c = 0; c < kCandPerLane; ++c) tk[c] = kk[c];
+            wt[j] = warp_max64_key(tree_max64(tk));
+#pragma unroll
+            for (int c = 0; c < kCandPerLane; ++c) kk[c] = kk[c] == wt[j] ? 0ull : kk[c];
+          }
+          if (kReplay > 1) {  // the best over the replay warps
+            const uint32_t par = iter & 1u;
+            if (lane == 0) {
+#pragma unroll
+              for (int j = 0; j < kSpec; ++j) ctl.xkey[par][warp][j] = wt[j];
+            }
+            replay_sync();
+            unsigned long long all[kReplay * kSpec];
+#pragma unroll
+            for (int w = 0; w < kReplay; ++w)
+#pragma unroll
+              for (int j = 0; j < kSpec; ++j) all[w * kSpec + j] = ctl.xkey[par][w][j];
+#pragma unroll
+            for (int j = 0; j < kSpec; ++j) {
+              unsigned long long tk[kReplay * kSpec];
+#pragma unroll
+              for (int e = 0; e < kReplay * kSpec; ++e) tk[e] = all[e];
+              wt[j] = tree_max64(tk);
+#pragma unroll
+              for (int e = 0; e < kReplay * kSpec; ++e) all[e] = all[e] == wt[j] ? 0ull : all[e];
+            }
+          }
+          ++iter;
+          if (wt[0] <= bstar) break;  // not certain: some unlisted point may win
+          float wx[kSpec], wy[kSpec], wz[kSpec], wd[kSpec];
+          uint32_t wcell[kSpec], wcube[kSpec][3];
+#pragma unroll
+          for (int j = 0; j < kSpec; ++j) {
+            const uint32_t slot = (uint32_t)wt[j] & 0xffu;
+            const Cand &qcd = ctl.live[slot];
+            const float4 qv = *reinterpret_cast<const float4 *>(&qcd.x);
+            wx[j] = qv.x; wy[j] = qv.y; wz[j] = qv.z;
+            wcell[j] = qcd.cell;
+            wd[j] = __uint_as_float((uint32_t)(wt[j] >> 32) - 1u);  // its current distance
+          }
+          if (!(wd[0] > 0.0f)) {  // src/yuezu_fps.cpp:705-706
             finished = true;
             break;
           }
-          const uint32_t qpos = 0xffffffffu - (uint32_t)wk;
-          const uint32_t qc[3] = {qcell & 1023u, (qcell >> 10) & 1023u, qcell >> 20};
-          uint32_t cube[3];
-          cube_of(ax, fast, qc, qd, cube);
-          if (lane == 0) {
-            Sample sm;
-            sm.q = make_float4(qx, qy, qz, qd);
-            sm.c = make_uint4(cube[0], cube[1], cube[2], qpos);
-            s_samp[n] = sm;
-            st_release_cta(&ctl.produced, n + 1);  // the workers may apply it now
+#pragma unroll
+          for (int j = 0; j < kSpec; ++j) {
+            const float qd = wd[j];
+            const uint32_t qc[3] = {wcell[j] & 1023u, (wcell[j] >> 10) & 1023u, wcell[j] >> 20};
+            if (regtab) {
+              const bool empty = qd > ax[0].ovf || qd > ax[1].ovf || qd > ax[2].ovf;
+#pragma unroll
+              for (int d = 0; d < 3; ++d) {
+                int nh = __popc(__ballot_sync(kFull, qd > rt[d][0]));
+                if (wide) nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
+                const int top = ax[d].blocks - 1;
+                const int l = (int)qc[d] - nh > 0 ? (int)qc[d] - nh : 0;
+                const int h = (int)qc[d] + nh < top ? (int)qc[d] + nh : top;
+                wcube[j][d] = empty ? kNoCell : ((uint32_t)l | ((uint32_t)(h - l) << 16));
+              }
+            } else {
+              cube_of(ax, fast, qc, qd, wcube[j]);
+            }
+          }
+          // the accepted prefix W0 .. W(m-1)
+          uint32_t m = 1;
+          bool ok = true;
+#pragma unroll
+          for (int j = 1; j < kSpec; ++j) {
+            ok = ok && wt[j] > bstar && wd[j] > 0.0f && it + (uint32_t)j < a.k &&
+                 n + (uint32_t)j < (uint32_t)kQueue;
+#pragma unroll
+            for (int i = 0; i < j; ++i)
+              ok = ok && wcube[i][0] != kNoCell &&
+                   !in_box(wcell[j], wcube[i][0], wcube[i][1], wcube[i][2]);
+            m += ok ? 1u : 0u;
+          }
+          if (warp == 0 && lane == 0) {
+#pragma unroll
+            for (int j = 0; j < kSpec; ++j)
+              if ((uint32_t)j < m) {
+                Sample sm;
+                sm.q = make_float4(wx[j], wy[j], wz[j], wd[j]);
+                sm.c = make_uint4(wcube[j][0], wcube[j][1], wcube[j][2],
+                                  pbase + (0xffffffu - ((uint32_t)wt[j] >> 8)));
+                s_samp[n + j] = sm;
+              }
+            st_release_cta(&ctl.produced, n + m);  // the workers may apply them now
           }
 #pragma unroll
-          for (int c = 0; c < kCandPerLane; ++c)
-            if (in_box(ccell[c], cube[0], cube[1], cube[2])) {
-              const float d = sqdist(cx[c], cy[c], cz[c], qx, qy, qz);
-              if (d < cdd[c]) cdd[c] = d;
+          for (int j = 0; j < kSpec; ++j)
+            if ((uint32_t)j < m) {
+#pragma unroll
+              for (int c = 0; c < kCandPerLane; ++c) {  // branch-free per candidate
+                if ((uint32_t)c >= rows) break;
+                const float d = sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]);
+                cdd[c] = (in_box(ccell[c], wcube[j][0], wcube[j][1], wcube[j][2]) && d < cdd[c])
+                             ? d : cdd[c];
+              }
             }
-          ++n;
-          ++it;
+          n += m;
+          it += m;
         }
         if (it >= a.k) finished = true;
       }
-      if (lane == 0) {
+      if (warp == 0 && lane == 0) {
+        st_release_cta(&ctl.produced, n);
         ctl.finished = finished ? 1u : 0u;
         st_release_cta(&ctl.done, 1u);
       }
-    }
- else {
+    } else {
       uint32_t s = 0;
       unsigned long long deadline = 0;
       uint32_t polls = 0;
@@ -547,11 +812,16 @@ fps_rounds_cluster(const LoopArgs a) {
         const uint32_t p = ld_acquire_cta(&ctl.produced);
         if (s < p) {
 #pragma unroll 1
-          for (; s < p; ++s) apply(s);
+          for (; s < p; s += kBatch) apply(s, min(p - s, (uint32_t)kBatch));
+          s = p;
           continue;
         }
         if (ld_acquire_cta(&ctl.done)) {
-          if (s >= ld_acquire_cta(&ctl.produced)) break;
+          if (s >= ld_acquire_cta(&ctl.produced)) {
+            out_n = s;
+            out_first = ctl.first;
+            break;
+          }
           continue;
         }
         __nanosleep(32);
@@ -563,12 +833,12 @@ fps_rounds_cluster(const LoopArgs a) {
       }
     }
     __syncthreads();  // every sample of the round applied
-    if (crank == 0) {  // the round's samples, written once the round is over
-      const uint32_t nq = ctl.produced, f = ctl.first;
-      for (uint32_t s2 = tid; s2 < nq; s2 += THREADS)
-        a.out_rank[(uint64_t)cloud * a.k + f + s2] = s_samp[s2].c.w;
-      __syncthreads();  // s_samp is rewritten by the next round
-    }
+    // CTA 0's workers write the round's samples out while warp 0 starts the
+    // next round; s_samp is rewritten only after the next round's first
+    // barrier, and the counts were read before this one
+    if (crank == 0 && warp >= kReplay)
+      for (uint32_t s2 = (uint32_t)(tid - 32 * kReplay); s2 < out_n; s2 += (uint32_t)kWorkers)
+        a.out_rank[(uint64_t)cloud * a.k + out_first + s2] = s_samp[s2].c.w;
     if (ctl.finished) break;
   }
 
@@ -644,7 +914,8 @@ int rounds_leaves_per_thread(uint32_t leaves) {
 }
 
 size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab) {
-  return (size_t)pts * 16 + (size_t)leaves * 32 + (size_t)((tab + 3) & ~3u) * 4 +
+  return (size_t)pts * 16 + (size_t)leaves * 32 + (size_t)((leaves + 3) & ~3u) * 4 +
+         (size_t)((tab + 3) & ~3u) * 4 +
          (size_t)kQueue * sizeof(Sample);
 }
 
