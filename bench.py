@@ -253,7 +253,7 @@ def run_ours(args):
     # ---- device-resident timed region
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    loop_ms, ref_pts, evals, launches, samples = 0.0, 0, 0, 0, 0
+    loop_ms, ref_pts, evals, launches, samples, loop_mode = 0.0, 0, 0, 0, 0, 0
     with ClockSampler(local) as clk:
         for s in range(args.steps):
             flush.zero_()  # L2 flush outside the timed window
@@ -265,6 +265,7 @@ def run_ours(args):
             ref_pts += prof.ref_points_updated
             evals += prof.points_evaluated
             launches += prof.launches
+            loop_mode = prof.mode
             samples += sum(lens)
         torch.cuda.synchronize(dev)
     step_ms = [a.elapsed_time(b) for a, b in ev]
@@ -320,7 +321,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": peak_kind,
-                         "kernel": "fps_loop_cluster",
+                         "kernel": "fps_rounds_cluster" if loop_mode == 2 else "fps_loop_cluster",
                          "algorithmic_bytes_per_launch": alg_bytes / args.steps,
                          "kernel_ms_per_launch": loop_ms / args.steps,
                          "points_evaluated_per_launch": evals / args.steps},

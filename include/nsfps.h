@@ -196,7 +196,8 @@ NSFPS_API int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k
  * counters of the sampling loop: points in the buckets the reference updates
  * (summed over iterations), points actually re-evaluated after the exact
  * bounding-box skip, and the loop configuration (CTAs per cloud and mode:
- * 0 = thread-block cluster, 1 = grid-wide).  Enabled by nsfps_set_profiling. */
+ * 0 = per-step cluster loop, 2 = round-based cluster loop).  Enabled by
+ * nsfps_set_profiling. */
 typedef struct nsfps_profile {
   float setup_ms, loop_ms, total_ms;
   uint32_t launches;

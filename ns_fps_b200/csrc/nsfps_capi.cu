@@ -569,7 +569,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     p.total_ms = ms;
     p.launches = launches;
     p.ctas_per_cloud = plan.P;
-    p.mode = (uint32_t)plan.mode;
+    p.mode = plan.rounds ? 2u : (uint32_t)plan.mode;
     p.leaves = hscal[kScalarLeaves];
     p.ref_points_updated = hstats[0];
     p.points_evaluated = hstats[1];

@@ -362,8 +362,10 @@ __global__ void plan_partition(const float4 *__restrict__ leaf_lo,
                                const uint32_t *__restrict__ loff, uint32_t B,
                                const uint32_t *__restrict__ cand, int ncand,
                                uint32_t total_ctas, uint32_t *__restrict__ plan) {
-  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total_ctas;
-       t += gridDim.x * blockDim.x) {
+  // one warp per (candidate CTA count, cloud, CTA); lanes stride its leaves
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < total_ctas; t += nwarps) {
     // decode t -> (candidate i, cloud c, cta j)
     uint32_t rem = t;
     int i = 0;
@@ -372,21 +374,26 @@ __global__ void plan_partition(const float4 *__restrict__ leaf_lo,
       if (rem < span) break;
       rem -= span;
     }
-    if (i >= ncand) continue;
+    if (i >= ncand) continue;  // uniform over the warp
     const uint32_t P = cand[i];
     const uint32_t c = rem / P, j = rem % P;
     const uint32_t l0 = loff[c], l1 = loff[c + 1];
     uint32_t pts = 0, leaves = 0, extra = 0;
-    for (uint32_t l = l0 + j; l < l1; l += P) {
+    for (uint32_t l = l0 + j + lane * P; l < l1; l += 32u * P) {
       const uint32_t w = __float_as_uint(leaf_lo[l].w);
       const uint32_t npre = w >> 16;
       pts += w & 0xffu;
       extra += npre > 1 ? npre - 1 : 0;
       ++leaves;
     }
-    atomicMax(&plan[3 * i], pts);
-    atomicMax(&plan[3 * i + 1], leaves);
-    atomicMax(&plan[3 * i + 2], extra);
+    pts = __reduce_add_sync(0xffffffffu, pts);
+    leaves = __reduce_add_sync(0xffffffffu, leaves);
+    extra = __reduce_add_sync(0xffffffffu, extra);
+    if (lane == 0) {
+      atomicMax(&plan[3 * i], pts);
+      atomicMax(&plan[3 * i + 1], leaves);
+      atomicMax(&plan[3 * i + 2], extra);
+    }
   }
 }
 
@@ -446,7 +453,7 @@ cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
   uint64_t total = 0;
   for (int i = 0; i < a.ncand; ++i) total += (uint64_t)a.cand_host[i] * B;
   if (total) {
-    const uint32_t blocks = (uint32_t)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+    const uint32_t blocks = (uint32_t)((total + 7) / 8 < 4096 ? (total + 7) / 8 : 4096);  // 8 warps each
     plan_partition<<<blocks, 256, 0, st>>>(a.leaf_lo, a.loff, B, a.cand, a.ncand,
                                            (uint32_t)total, a.plan);
     launches += 1;
