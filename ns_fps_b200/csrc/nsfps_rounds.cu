@@ -50,8 +50,29 @@ namespace {
 #define NSFPS_REPLAY_WARPS 2
 #endif
 constexpr int kReplay = NSFPS_REPLAY_WARPS;
-constexpr int kWarps = kLoopThreads / 32;
-constexpr int kWorkers = kLoopThreads - 32 * kReplay;  // leaf-owning threads
+// Threads per CTA of this kernel (a build-time choice, a multiple of 32 up
+// to 512); above 256 a thread owns at most 4 leaves (registers).
+#ifndef NSFPS_ROUND_THREADS
+#define NSFPS_ROUND_THREADS 256
+#endif
+constexpr int kRoundThreads = NSFPS_ROUND_THREADS;
+constexpr int kMaxLeavesPerThread = kRoundThreads > 256 ? 4 : 8;
+constexpr int kWarps = kRoundThreads / 32;
+// Optionally the replay warps' partners on their SM sub-partitions (warp
+// r + 4 shares its scheduler with warp r) stay idle.
+#ifndef NSFPS_IDLE_PARTNER
+#define NSFPS_IDLE_PARTNER 0
+#endif
+constexpr int kIdle = NSFPS_IDLE_PARTNER ? kReplay : 0;
+constexpr int kWorkers = kRoundThreads - 32 * (kReplay + kIdle);  // leaf-owning threads
+static_assert(kIdle == 0 || (kRoundThreads == 256 && kReplay <= 2), "idle partners: 8 warps");
+
+// Index of a leaf-owning warp among the workers; -1 for replay and idle warps.
+__device__ __forceinline__ int worker_index(int warp) {
+  if (warp < kReplay) return -1;
+  if (kIdle && warp >= 4 && warp < 4 + kIdle) return -1;
+  return warp - kReplay - ((kIdle && warp >= 4 + kIdle) ? kIdle : 0);
+}
 constexpr int kMaxCands = 256;                          // P * T
 constexpr int kCandPerLane = kMaxCands / (32 * kReplay);
 constexpr int kQueue = 512;                    // samples decided per round, at most
@@ -172,9 +193,9 @@ __device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
 }
 
 template <int M, int T>
-__global__ void __launch_bounds__(kLoopThreads, 1)
+__global__ void __launch_bounds__(kRoundThreads, 1)
 fps_rounds_cluster(const LoopArgs a) {
-  constexpr int THREADS = kLoopThreads;
+  constexpr int THREADS = kRoundThreads;
   constexpr int W = kWarps;
   extern __shared__ float4 smem[];
   __shared__ RoundCtl<T> ctl;
@@ -276,10 +297,11 @@ fps_rounds_cluster(const LoopArgs a) {
   // order), as slots of 32: leaf m * 32 + lane of the run is its lane's m-th.
   constexpr uint32_t kWorkerWarps = (uint32_t)kWorkers / 32u;
   const uint32_t span = (nl + kWorkerWarps - 1u) / kWorkerWarps;
-  const uint32_t wbase = warp >= kReplay ? (uint32_t)(warp - kReplay) * span : 0u;
+  const int widx = worker_index(warp);
+  const uint32_t wbase = widx >= 0 ? (uint32_t)widx * span : 0u;
   auto owned = [&](int m, uint32_t ln) {
     const uint32_t r = (uint32_t)m * 32u + ln;
-    return warp >= kReplay && r < span && wbase + r < nl;
+    return widx >= 0 && r < span && wbase + r < nl;
   };
   uint32_t cell[M], cnt[M], gst[M], gpos[M], sbox_lo[M], sbox_hi[M];
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
@@ -361,21 +383,28 @@ fps_rounds_cluster(const LoopArgs a) {
       live |= cube_misses(cb.x, cb.y, cb.z, wbox_lo, wbox_hi) ? 0u : (1u << j);
     }
     if (live == 0u) return;
+    // slots whose cell box the cubes reach (uniform over the warp)
+    uint32_t act[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      act[m] = 0u;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        act[m] |= (((live >> j) & 1u) &&
+                   !cube_misses(c0[j], c1[j], c2[j], sbox_lo[m], sbox_hi[m])) ? (1u << j) : 0u;
+    }
     uint32_t needb[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       needb[m] = 0u;
+      if (act[m] == 0u) continue;
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        if (!((live >> j) & 1u) || cube_misses(c0[j], c1[j], c2[j], sbox_lo[m], sbox_hi[m]))
-          continue;
-        const bool hit = in_box(cell[m], c0[j], c1[j], c2[j]);
-        const float gx = qx[j] < bx0[m] ? __fsub_rn(bx0[m], qx[j])
-                                        : (qx[j] > bx1[m] ? __fsub_rn(qx[j], bx1[m]) : 0.0f);
-        const float gy = qy[j] < by0[m] ? __fsub_rn(by0[m], qy[j])
-                                        : (qy[j] > by1[m] ? __fsub_rn(qy[j], by1[m]) : 0.0f);
-        const float gz = qz[j] < bz0[m] ? __fsub_rn(bz0[m], qz[j])
-                                        : (qz[j] > bz1[m] ? __fsub_rn(qz[j], bz1[m]) : 0.0f);
+        const bool hit = ((act[m] >> j) & 1u) && in_box(cell[m], c0[j], c1[j], c2[j]);
+        // distance from the sample to the leaf box, per axis (0 inside)
+        const float gx = fmaxf(fmaxf(__fsub_rn(bx0[m], qx[j]), __fsub_rn(qx[j], bx1[m])), 0.0f);
+        const float gy = fmaxf(fmaxf(__fsub_rn(by0[m], qy[j]), __fsub_rn(qy[j], by1[m])), 0.0f);
+        const float gz = fmaxf(fmaxf(__fsub_rn(bz0[m], qz[j]), __fsub_rn(qz[j], bz1[m])), 0.0f);
         const float lbd =
             __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
         const bool need = hit && lbd < lmax[m];
@@ -441,7 +470,7 @@ fps_rounds_cluster(const LoopArgs a) {
 
     // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum, in
     // order (keys are unique: every leaf has its own sorted position)
-    if (warp >= kReplay) {
+    if (widx >= 0) {
       unsigned long long lk[M];
       int rk[M];
 #pragma unroll
@@ -449,7 +478,7 @@ fps_rounds_cluster(const LoopArgs a) {
         lk[m] = pkey(lmax[m], gpos[m]);  // 0 for a leaf this lane does not own
         rk[m] = -1;
       }
-      if (lane <= T) ctl.wkey[warp][lane] = 0ull;
+      if (lane <= T) ctl.wkey[widx][lane] = 0ull;
 #pragma unroll 1
       for (int t = 0; t <= T; ++t) {
         unsigned long long tk[M];
@@ -465,8 +494,8 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
       for (int m = 0; m < M; ++m)
         if (rk[m] >= 0) {
-          ctl.wkey[warp][rk[m]] = pkey(lmax[m], gpos[m]);
-          ctl.wleaf[warp][rk[m]] = wbase + (uint32_t)m * 32u + (uint32_t)lane;
+          ctl.wkey[widx][rk[m]] = pkey(lmax[m], gpos[m]);
+          ctl.wleaf[widx][rk[m]] = wbase + (uint32_t)m * 32u + (uint32_t)lane;
         }
     } else if (warp == 0 && lane == 0) {
       ctl.produced = 0u;
@@ -480,15 +509,15 @@ fps_rounds_cluster(const LoopArgs a) {
     if (warp < kReplay) {
       if (warp == 0) {
         // merge the worker warps' lists ((W - kReplay) * (T+1) entries)
-        constexpr int NE = (W - kReplay) * (T + 1);
+        constexpr int NE = (kWorkers / 32) * (T + 1);
         constexpr int E = (NE + 31) / 32;
         unsigned long long ek[E];
         uint32_t el[E];
 #pragma unroll
         for (int e = 0; e < E; ++e) {
           const int idx = lane + 32 * e;
-          ek[e] = idx < NE ? ctl.wkey[kReplay + idx / (T + 1)][idx % (T + 1)] : 0ull;
-          el[e] = idx < NE ? ctl.wleaf[kReplay + idx / (T + 1)][idx % (T + 1)] : 0u;
+          ek[e] = idx < NE ? ctl.wkey[idx / (T + 1)][idx % (T + 1)] : 0ull;
+          el[e] = idx < NE ? ctl.wleaf[idx / (T + 1)][idx % (T + 1)] : 0u;
         }
         int er[E];
 #pragma unroll
@@ -804,7 +833,7 @@ fps_rounds_cluster(const LoopArgs a) {
         ctl.finished = finished ? 1u : 0u;
         st_release_cta(&ctl.done, 1u);
       }
-    } else {
+    } else if (widx >= 0) {
       uint32_t s = 0;
       unsigned long long deadline = 0;
       uint32_t polls = 0;
@@ -836,8 +865,8 @@ fps_rounds_cluster(const LoopArgs a) {
     // CTA 0's workers write the round's samples out while warp 0 starts the
     // next round; s_samp is rewritten only after the next round's first
     // barrier, and the counts were read before this one
-    if (crank == 0 && warp >= kReplay)
-      for (uint32_t s2 = (uint32_t)(tid - 32 * kReplay); s2 < out_n; s2 += (uint32_t)kWorkers)
+    if (crank == 0 && widx >= 0)
+      for (uint32_t s2 = (uint32_t)(widx * 32 + lane); s2 < out_n; s2 += (uint32_t)kWorkers)
         a.out_rank[(uint64_t)cloud * a.k + out_first + s2] = s_samp[s2].c.w;
     if (ctl.finished) break;
   }
@@ -876,7 +905,7 @@ cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B * a.P, 1, 1);
-  cfg.blockDim = dim3(kLoopThreads, 1, 1);
+  cfg.blockDim = dim3(kRoundThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -896,8 +925,10 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
     case 2: return launch_rounds<2, T>(a, smem, st);
     case 3: return launch_rounds<3, T>(a, smem, st);
     case 4: return launch_rounds<4, T>(a, smem, st);
-    case 6: return launch_rounds<6, T>(a, smem, st);
-    case 8: return launch_rounds<8, T>(a, smem, st);
+    case 6: return kMaxLeavesPerThread >= 6 ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T>(a, smem, st)
+                                            : cudaErrorInvalidValue;
+    case 8: return kMaxLeavesPerThread >= 8 ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T>(a, smem, st)
+                                            : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
@@ -909,7 +940,7 @@ int rounds_candidates_per_cta(uint32_t) { return 16; }
 int rounds_leaves_per_thread(uint32_t leaves) {
   static const int ms[] = {1, 2, 3, 4, 6, 8};
   for (int m : ms)
-    if ((uint32_t)m * kWorkers >= leaves) return m;
+    if (m <= kMaxLeavesPerThread && (uint32_t)m * kWorkers >= leaves) return m;
   return 0;
 }
 
