@@ -304,6 +304,7 @@ fps_rounds_cluster(const LoopArgs a) {
     return widx >= 0 && r < span && wbase + r < nl;
   };
   uint32_t cell[M], cnt[M], gst[M], gpos[M], sbox_lo[M], sbox_hi[M];
+  uint32_t lsc[M];  // shared-memory start | count << 16
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
   uint32_t wx0 = 1023u, wy0 = 1023u, wz0 = 1023u, wx1 = 0u, wy1 = 0u, wz1 = 0u;
 #pragma unroll
@@ -316,6 +317,7 @@ fps_rounds_cluster(const LoopArgs a) {
       const uint32_t slot = (w >> 8) & 0xffu;
       cell[m] = __float_as_uint(hi.w);
       cnt[m] = w & 0xffu;
+      lsc[m] = (__float_as_uint(s_lo[i].w) & 0xffffu) | (cnt[m] << 16);
       gst[m] = a.leaf_start[g];
       lmax[m] = a.leaf_md[g];
       gpos[m] = gst[m] + slot;
@@ -324,6 +326,7 @@ fps_rounds_cluster(const LoopArgs a) {
     } else {
       cell[m] = 0xffffffffu;  // z field 4095: outside every cube
       cnt[m] = 0;
+      lsc[m] = 0u;
       gst[m] = 0;
       lmax[m] = -1.0f;
       gpos[m] = 0xffffffffu;
@@ -427,27 +430,23 @@ fps_rounds_cluster(const LoopArgs a) {
           lb2 = __ffs(mask) - 1;
           mask &= mask - 1;
         }
-        // half-warp h updates leaf la (h = 0) or lb2 (h = 1), a point per lane
+        // half-warp h updates leaf la (h = 0) or lb2 (h = 1), a point per
+        // lane; the owner's start, count and sample bits come in one shuffle
         const int src = half ? lb2 : la;
-        const uint32_t nbits = __shfl_sync(kFull, needb[m], src < 0 ? 0 : src);
-        uint32_t key = 0u;
-        if (src >= 0) {
-          const uint32_t l = wbase + (uint32_t)m * 32u + (uint32_t)src;
-          const uint32_t lw = __float_as_uint(s_lo[l].w);
-          const uint32_t start = lw & 0xffffu, c = lw >> 16;
-          if ((uint32_t)j16 < c) {
-            float4 p = s_pts[start + j16];
-            float w = p.w;
+        const uint32_t word =
+            __shfl_sync(kFull, lsc[m] | (needb[m] << 24), src < 0 ? la : src);
+        const uint32_t start = word & 0xffffu, c = (word >> 16) & 0xffu, nbits = word >> 24;
+        const bool on = src >= 0 && (uint32_t)j16 < c;
+        const uint32_t pi = start + (on ? (uint32_t)j16 : 0u);  // inside the leaf
+        const float4 p = s_pts[pi];
+        float w = p.w;
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j)
-              if ((nbits >> j) & 1u) {
-                const float d = sqdist(p.x, p.y, p.z, qx[j], qy[j], qz[j]);
-                if (d < w) w = d;
-              }
-            if (w < p.w) s_pts[start + j16].w = w;
-            key = dkey(w);
-          }
+        for (int j = 0; j < kBatch; ++j) {
+          const float d = sqdist(p.x, p.y, p.z, qx[j], qy[j], qz[j]);
+          w = (((nbits >> j) & 1u) && d < w) ? d : w;
         }
+        if (on && w < p.w) s_pts[pi].w = w;
+        const uint32_t key = on ? dkey(w) : 0u;
         const uint32_t kA = __reduce_max_sync(kFull, half ? 0u : key);
         const uint32_t kB = __reduce_max_sync(kFull, half ? key : 0u);
         const uint32_t fA = __ffs(__ballot_sync(kFull, !half && key == kA)) - 1;
