@@ -119,6 +119,15 @@ __device__ __forceinline__ void st_release_cta(uint32_t *p, uint32_t v) {
   asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
 }
 
+// The same, by the threads whose `pred` holds (no divergent branch).
+__device__ __forceinline__ void st_release_cta_if(bool pred, uint32_t *p, uint32_t v) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.release.cta.shared.u32 [%0], %1;\n\t}" ::"r"(
+          smem_u32(p)),
+      "r"(v), "r"((uint32_t)pred)
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");

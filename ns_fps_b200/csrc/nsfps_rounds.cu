@@ -38,6 +38,8 @@
 //
 // Buffers rotate over four rounds (a CTA publishes round r+1 only after it
 // has every round-r list), waits are bounded by %globaltimer.
+#include <type_traits>
+
 #include "nsfps_device.cuh"
 
 namespace nsfps {
@@ -713,118 +715,125 @@ fps_rounds_cluster(const LoopArgs a) {
         // to 0, so after them Wj is the largest key, exactly as in the
         // reference; the candidates' updates commute (min).
         uint32_t iter = 0;
-        while (it < a.k && n < (uint32_t)kQueue) {
-          unsigned long long kk[kCandPerLane];
+        // the loop, with the cube source fixed (no branch on it per step)
+        auto replay = [&](auto use_regtab) {
+          constexpr bool kRegTab = decltype(use_regtab)::value;
+          for (;;) {
+            unsigned long long kk[kCandPerLane];
 #pragma unroll
-          for (int c = 0; c < kCandPerLane; ++c)
-            kk[c] = (uint32_t)c < rows ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
-          unsigned long long wt[kSpec];  // this warp's best keys, in order
-#pragma unroll
-          for (int j = 0; j < kSpec; ++j) {
-            unsigned long long tk[kCandPerLane];
-#pragma unroll
-            for (int c = 0; c < kCandPerLane; ++c) tk[c] = kk[c];
-            wt[j] = warp_max64_key(tree_max64(tk));
-#pragma unroll
-            for (int c = 0; c < kCandPerLane; ++c) kk[c] = kk[c] == wt[j] ? 0ull : kk[c];
-          }
-          if (kReplay > 1) {  // the best over the replay warps
-            const uint32_t par = iter & 1u;
-            if (lane == 0) {
-#pragma unroll
-              for (int j = 0; j < kSpec; ++j) ctl.xkey[par][warp][j] = wt[j];
-            }
-            replay_sync();
-            unsigned long long all[kReplay * kSpec];
-#pragma unroll
-            for (int w = 0; w < kReplay; ++w)
-#pragma unroll
-              for (int j = 0; j < kSpec; ++j) all[w * kSpec + j] = ctl.xkey[par][w][j];
+            for (int c = 0; c < kCandPerLane; ++c)
+              kk[c] = (uint32_t)c < rows ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
+            unsigned long long wt[kSpec];  // this warp's best keys, in order
 #pragma unroll
             for (int j = 0; j < kSpec; ++j) {
-              unsigned long long tk[kReplay * kSpec];
+              unsigned long long tk[kCandPerLane];
 #pragma unroll
-              for (int e = 0; e < kReplay * kSpec; ++e) tk[e] = all[e];
-              wt[j] = tree_max64(tk);
+              for (int c = 0; c < kCandPerLane; ++c) tk[c] = kk[c];
+              wt[j] = warp_max64_key(tree_max64(tk));
 #pragma unroll
-              for (int e = 0; e < kReplay * kSpec; ++e) all[e] = all[e] == wt[j] ? 0ull : all[e];
+              for (int c = 0; c < kCandPerLane; ++c) kk[c] = kk[c] == wt[j] ? 0ull : kk[c];
             }
-          }
-          ++iter;
-          if (wt[0] <= bstar) break;  // not certain: some unlisted point may win
-          float wx[kSpec], wy[kSpec], wz[kSpec], wd[kSpec];
-          uint32_t wcell[kSpec], wcube[kSpec][3];
+            if (kReplay > 1) {  // the best over the replay warps
+              const uint32_t par = iter & 1u;
+              // every lane stores the same keys: no divergent branch
 #pragma unroll
-          for (int j = 0; j < kSpec; ++j) {
-            const uint32_t slot = (uint32_t)wt[j] & 0xffu;
-            const Cand &qcd = ctl.live[slot];
-            const float4 qv = *reinterpret_cast<const float4 *>(&qcd.x);
-            wx[j] = qv.x; wy[j] = qv.y; wz[j] = qv.z;
-            wcell[j] = qcd.cell;
-            wd[j] = __uint_as_float((uint32_t)(wt[j] >> 32) - 1u);  // its current distance
-          }
-          if (!(wd[0] > 0.0f)) {  // src/yuezu_fps.cpp:705-706
-            finished = true;
-            break;
-          }
+              for (int j = 0; j < kSpec; ++j) ctl.xkey[par][warp][j] = wt[j];
+              replay_sync();
+              unsigned long long all[kReplay * kSpec];
 #pragma unroll
-          for (int j = 0; j < kSpec; ++j) {
-            const float qd = wd[j];
-            const uint32_t qc[3] = {wcell[j] & 1023u, (wcell[j] >> 10) & 1023u, wcell[j] >> 20};
-            if (regtab) {
-              const bool empty = qd > ax[0].ovf || qd > ax[1].ovf || qd > ax[2].ovf;
+              for (int w = 0; w < kReplay; ++w)
 #pragma unroll
-              for (int d = 0; d < 3; ++d) {
-                int nh = __popc(__ballot_sync(kFull, qd > rt[d][0]));
-                if (wide) nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
-                const int top = ax[d].blocks - 1;
-                const int l = (int)qc[d] - nh > 0 ? (int)qc[d] - nh : 0;
-                const int h = (int)qc[d] + nh < top ? (int)qc[d] + nh : top;
-                wcube[j][d] = empty ? kNoCell : ((uint32_t)l | ((uint32_t)(h - l) << 16));
+                for (int j = 0; j < kSpec; ++j) all[w * kSpec + j] = ctl.xkey[par][w][j];
+#pragma unroll
+              for (int j = 0; j < kSpec; ++j) {
+                unsigned long long tk[kReplay * kSpec];
+#pragma unroll
+                for (int e = 0; e < kReplay * kSpec; ++e) tk[e] = all[e];
+                wt[j] = tree_max64(tk);
+#pragma unroll
+                for (int e = 0; e < kReplay * kSpec; ++e) all[e] = all[e] == wt[j] ? 0ull : all[e];
               }
-            } else {
-              cube_of(ax, fast, qc, qd, wcube[j]);
             }
-          }
-          // the accepted prefix W0 .. W(m-1)
-          uint32_t m = 1;
-          bool ok = true;
+            ++iter;
+            float wd[kSpec];
 #pragma unroll
-          for (int j = 1; j < kSpec; ++j) {
-            ok = ok && wt[j] > bstar && wd[j] > 0.0f && it + (uint32_t)j < a.k &&
-                 n + (uint32_t)j < (uint32_t)kQueue;
+            for (int j = 0; j < kSpec; ++j)
+              wd[j] = __uint_as_float((uint32_t)(wt[j] >> 32) - 1u);  // current distance
+            // stop when some unlisted point may win (not certain), or when the
+            // best distance is 0 (src/yuezu_fps.cpp:705-706)
+            if (!(wt[0] > bstar && wd[0] > 0.0f)) {
+              finished = wt[0] > bstar;
+              break;
+            }
+            float wx[kSpec], wy[kSpec], wz[kSpec];
+            uint32_t wcell[kSpec], wcube[kSpec][3];
 #pragma unroll
-            for (int i = 0; i < j; ++i)
-              ok = ok && wcube[i][0] != kNoCell &&
-                   !in_box(wcell[j], wcube[i][0], wcube[i][1], wcube[i][2]);
-            m += ok ? 1u : 0u;
-          }
-          if (warp == 0 && lane == 0) {
+            for (int j = 0; j < kSpec; ++j) {
+              const Cand &qcd = ctl.live[(uint32_t)wt[j] & 0xffu];
+              const float4 qv = *reinterpret_cast<const float4 *>(&qcd.x);
+              wx[j] = qv.x; wy[j] = qv.y; wz[j] = qv.z;
+              wcell[j] = qcd.cell;
+            }
+#pragma unroll
+            for (int j = 0; j < kSpec; ++j) {
+              const float qd = wd[j];
+              const uint32_t qc[3] = {wcell[j] & 1023u, (wcell[j] >> 10) & 1023u, wcell[j] >> 20};
+              if (kRegTab) {
+                const bool empty = qd > ax[0].ovf || qd > ax[1].ovf || qd > ax[2].ovf;
+#pragma unroll
+                for (int d = 0; d < 3; ++d) {
+                  int nh = __popc(__ballot_sync(kFull, qd > rt[d][0]));
+                  if (wide) nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
+                  const int top = ax[d].blocks - 1;
+                  const int l = (int)qc[d] - nh > 0 ? (int)qc[d] - nh : 0;
+                  const int h = (int)qc[d] + nh < top ? (int)qc[d] + nh : top;
+                  wcube[j][d] = empty ? kNoCell : ((uint32_t)l | ((uint32_t)(h - l) << 16));
+                }
+              } else {
+                cube_of(ax, fast, qc, qd, wcube[j]);
+              }
+            }
+            // the accepted prefix W0 .. W(m-1)
+            uint32_t m = 1;
+            bool ok = true;
+#pragma unroll
+            for (int j = 1; j < kSpec; ++j) {
+              ok = ok && wt[j] > bstar && wd[j] > 0.0f && it + (uint32_t)j < a.k &&
+                   n + (uint32_t)j < (uint32_t)kQueue;
+#pragma unroll
+              for (int i = 0; i < j; ++i)
+                ok = ok && wcube[i][0] != kNoCell &&
+                     !in_box(wcell[j], wcube[i][0], wcube[i][1], wcube[i][2]);
+              m += ok ? 1u : 0u;
+            }
+            if (warp == 0) {  // queue the samples (every lane stores the same values)
+#pragma unroll
+              for (int j = 0; j < kSpec; ++j)
+                if ((uint32_t)j < m) {
+                  Sample sm;
+                  sm.q = make_float4(wx[j], wy[j], wz[j], wd[j]);
+                  sm.c = make_uint4(wcube[j][0], wcube[j][1], wcube[j][2],
+                                    pbase + (0xffffffu - ((uint32_t)wt[j] >> 8)));
+                  s_samp[n + j] = sm;
+                }
+              st_release_cta_if(lane == 0, &ctl.produced, n + m);  // the workers may apply them
+            }
 #pragma unroll
             for (int j = 0; j < kSpec; ++j)
               if ((uint32_t)j < m) {
-                Sample sm;
-                sm.q = make_float4(wx[j], wy[j], wz[j], wd[j]);
-                sm.c = make_uint4(wcube[j][0], wcube[j][1], wcube[j][2],
-                                  pbase + (0xffffffu - ((uint32_t)wt[j] >> 8)));
-                s_samp[n + j] = sm;
+#pragma unroll
+                for (int c = 0; c < kCandPerLane; ++c) {  // branch-free per candidate
+                  const float d = sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]);
+                  cdd[c] = (in_box(ccell[c], wcube[j][0], wcube[j][1], wcube[j][2]) && d < cdd[c])
+                               ? d : cdd[c];
+                }
               }
-            st_release_cta(&ctl.produced, n + m);  // the workers may apply them now
+            n += m;
+            it += m;
+            if (it >= a.k || n >= (uint32_t)kQueue) break;
           }
-#pragma unroll
-          for (int j = 0; j < kSpec; ++j)
-            if ((uint32_t)j < m) {
-#pragma unroll
-              for (int c = 0; c < kCandPerLane; ++c) {  // branch-free per candidate
-                if ((uint32_t)c >= rows) break;
-                const float d = sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]);
-                cdd[c] = (in_box(ccell[c], wcube[j][0], wcube[j][1], wcube[j][2]) && d < cdd[c])
-                             ? d : cdd[c];
-              }
-            }
-          n += m;
-          it += m;
-        }
+        };
+        if (regtab) replay(std::true_type{}); else replay(std::false_type{});
         if (it >= a.k) finished = true;
       }
       if (warp == 0 && lane == 0) {
