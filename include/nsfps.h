@@ -196,8 +196,9 @@ NSFPS_API int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k
  * counters of the sampling loop: points in the buckets the reference updates
  * (summed over iterations), points actually re-evaluated after the exact
  * bounding-box skip, and the loop configuration (CTAs per cloud and mode:
- * 0 = per-step cluster loop, 2 = round-based cluster loop).  Enabled by
- * nsfps_set_profiling. */
+ * 0 = per-step cluster loop, 2 = round-based cluster loop, 3 = round-based
+ * loop over co-resident CTAs for one cloud larger than a cluster's shared
+ * memory).  Enabled by nsfps_set_profiling. */
 typedef struct nsfps_profile {
   float setup_ms, loop_ms, total_ms;
   uint32_t launches;

@@ -278,10 +278,16 @@ struct Buffers {
   uint32_t *out_rank, *out_count;
   uint64_t *out;
   unsigned long long *stats;
+  uint4 *glist;
+  uint32_t *gbar;
 };
 
-constexpr uint32_t kClusterCand[] = {1, 2, 4, 8, 16};
-constexpr int kNumCand = 5;
+// CTAs per cloud the setup plans for: cluster sizes (one thread-block
+// cluster per cloud), then grid-wide sizes (one cloud over co-resident CTAs).
+constexpr uint32_t kClusterCand[] = {1, 2, 4, 8, 16, 32, 64, 128};
+constexpr int kNumCand = 8;
+constexpr int kNumCluster = 5;
+constexpr uint32_t kMaxGridP = 128;
 
 size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   const size_t n = j.n;
@@ -316,6 +322,8 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   b.out_count = c.take<uint32_t>(j.B);
   b.out = own_out ? c.take<uint64_t>((size_t)j.B * j.k) : nullptr;
   b.stats = c.take<unsigned long long>(4);
+  b.glist = j.B == 1 ? c.take<uint4>(rounds_grid_list_bytes(kMaxGridP) / 16) : nullptr;
+  b.gbar = j.B == 1 ? c.take<uint32_t>(1) : nullptr;
   return align_up(c.off, 256);
 }
 
@@ -482,7 +490,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   size_t bytes_sel = 0;
   auto select = [&]() {
     pi = -1;
-    for (int i = 0; i < kNumCand; ++i) {
+    for (int i = 0; i < kNumCluster; ++i) {
       int m;
       size_t bytes;
       if (!fits(i, m, bytes)) continue;
@@ -499,13 +507,29 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     rounds = false;
     select();
   }
+  // one cloud too large for a cluster: the grid-wide round loop over P
+  // co-resident CTAs (one per SM), the smallest P that fits
+  bool grid = false;
+  if (pi < 0 && j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist) {
+    rounds = true;
+    for (int i = kNumCluster; i < kNumCand && pi < 0; ++i) {
+      const uint32_t P = kClusterCand[i];
+      if (P > (uint32_t)sms || P > kMaxGridP || rounds_grid_candidates_per_cta(P) == 0) continue;
+      int m;
+      size_t bytes;
+      if (fits(i, m, bytes)) {
+        pi = i; m_sel = m; bytes_sel = bytes; grid = true;
+      }
+    }
+    if (!grid) rounds = !j.any_hashed && !g_force_steps.load();
+  }
   if (pi < 0)
     return set_error(NSFPS_ERR_UNSUPPORTED,
                      "cloud too large for the shared-memory-resident sampler "
-                     "(largest cloud part needs more than %d bytes at 16 CTAs)",
-                     max_smem);
+                     "(largest cloud part needs more than %d bytes at %u CTAs)",
+                     max_smem, j.B == 1 ? std::min<uint32_t>(kMaxGridP, (uint32_t)sms) : 16u);
   LoopPlan plan{};
-  plan.mode = 0;
+  plan.mode = grid ? 1 : 0;
   plan.rounds = rounds ? 1 : 0;
   plan.P = kClusterCand[pi];
   plan.leaves_per_thread = m_sel;
@@ -535,6 +559,8 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   la.out_count = b.out_count;
   la.scalars = b.scalars;
   la.stats = b.stats;
+  la.glist = b.glist;
+  la.gbar = b.gbar;
   la.timeout_ns = 2000000000ll;
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[2], st));
   NSFPS_CUDA(plan.rounds ? run_rounds(la, plan, st, launches) : run_loop(la, plan, st, launches));
@@ -569,7 +595,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     p.total_ms = ms;
     p.launches = launches;
     p.ctas_per_cloud = plan.P;
-    p.mode = plan.rounds ? 2u : (uint32_t)plan.mode;
+    p.mode = plan.rounds ? (plan.mode == 1 ? 3u : 2u) : (uint32_t)plan.mode;
     p.leaves = hscal[kScalarLeaves];
     p.ref_points_updated = hstats[0];
     p.points_evaluated = hstats[1];
@@ -647,6 +673,21 @@ int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
   std::vector<uint32_t> lens;
   std::vector<uint64_t> hout;
   rc = run_job(ctx, ctx->stream, j, nullptr, gc.data(), nullptr, nullptr, lens, &hout);
+  if (rc == NSFPS_ERR_UNSUPPORTED && gpu_idx.size() > 1) {
+    // a cloud too large to share the device with the others: one job per
+    // cloud (a single cloud may use the grid-wide loop)
+    for (size_t c = 0; c < gpu_idx.size(); ++c) {
+      Job j1;
+      rc = build_job(&gn[c], 1, k, ranges, std::vector<uint32_t>(1, grid[c]), j1);
+      if (rc) return rc;
+      rc = run_job(ctx, ctx->stream, j1, nullptr, &gc[c], nullptr, nullptr, lens, &hout);
+      if (rc) return rc;
+      const uint64_t i = gpu_idx[c];
+      std::memcpy(out[i], hout.data(), sizeof(uint64_t) * lens[0]);
+      out_len[i] = lens[0];
+    }
+    return NSFPS_OK;
+  }
   if (rc) return rc;
   for (size_t c = 0; c < gpu_idx.size(); ++c) {
     const uint64_t i = gpu_idx[c];

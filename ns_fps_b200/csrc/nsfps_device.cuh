@@ -128,6 +128,13 @@ __device__ __forceinline__ void st_release_cta_if(bool pred, uint32_t *p, uint32
       : "memory");
 }
 
+// Acquire load of a global word, GPU scope.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");

@@ -78,14 +78,14 @@ struct LoopArgs {
   uint32_t *out_count;        // B
   uint32_t *scalars;
   unsigned long long *stats;  // [0] reference-updated points, [1] evaluated
-  float4 *xslot;              // grid-wide mode: 2 * B * P exchange slots
-  uint32_t *xtag;             // grid-wide mode: 2 * B * P tags
+  uint4 *glist;               // grid-wide rounds: 2 * P published lists (global)
+  uint32_t *gbar;             // grid-wide rounds: arrival counter (starts at 0)
   long long timeout_ns;
 };
 
 // Which shared-memory-resident sampling kernel to run.
 struct LoopPlan {
-  int mode;          // 0 = thread-block cluster (P <= 16), 1 = grid-wide
+  int mode;          // 0 = thread-block cluster (P <= 16), 1 = grid-wide (rounds only)
   int rounds;        // 1 = exchange rounds of candidates (nsfps_rounds.cu)
   uint32_t P;
   int leaves_per_thread;  // template instance (1, 2, 3, 4, 6, 8)
@@ -105,6 +105,10 @@ size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab);
 int rounds_max_smem(uint32_t P);
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                        uint32_t &launches);
+// Grid-wide rounds (one cloud over P co-resident CTAs, lists through global
+// memory): candidates per CTA and the bytes of the global list buffers.
+int rounds_grid_candidates_per_cta(uint32_t P);
+size_t rounds_grid_list_bytes(uint32_t P);
 
 cudaError_t run_loop(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                      uint32_t &launches);

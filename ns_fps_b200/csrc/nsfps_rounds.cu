@@ -132,16 +132,6 @@ __device__ __forceinline__ unsigned long long pkey(float d, uint32_t pos) {
   return ((unsigned long long)dkey(d) << 32) | (unsigned long long)(0xffffffffu - pos);
 }
 
-// Largest 64-bit key over the warp; returns the lane holding it (lowest lane
-// among equal keys) and the key.
-__device__ __forceinline__ unsigned long long warp_max64(unsigned long long k, int &who) {
-  const uint32_t hi = (uint32_t)(k >> 32), lo = (uint32_t)k;
-  const uint32_t mh = __reduce_max_sync(kFull, hi);
-  const uint32_t ml = __reduce_max_sync(kFull, hi == mh ? lo : 0u);
-  who = __ffs(__ballot_sync(kFull, hi == mh && lo == ml)) - 1;
-  return ((unsigned long long)mh << 32) | ml;
-}
-
 // In-register maximum of N keys (a tree; the array is overwritten).
 template <int N>
 __device__ __forceinline__ unsigned long long tree_max64(unsigned long long (&k)[N]) {
@@ -180,6 +170,20 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   return m;
 }
 
+// A candidate from a list in shared memory, or from the global list buffer
+// (read at L2, past this SM's L1: the slot was rewritten by another SM).
+template <bool GRID>
+__device__ __forceinline__ Cand load_cand(const Cand *p) {
+  if (!GRID) return *p;
+  const uint4 *q = reinterpret_cast<const uint4 *>(p);
+  const uint4 v0 = __ldcg(q), v1 = __ldcg(q + 1);
+  Cand c;
+  c.x = __uint_as_float(v0.x); c.y = __uint_as_float(v0.y); c.z = __uint_as_float(v0.z);
+  c.d = __uint_as_float(v0.w);
+  c.pos = v1.x; c.cell = v1.y; c.pad0 = v1.z; c.pad1 = v1.w;
+  return c;
+}
+
 // Barrier of the replay warps alone (barrier 0 is __syncthreads).
 __device__ __forceinline__ void replay_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(32 * kReplay) : "memory");
@@ -194,11 +198,13 @@ __device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
   return ((0xffffffu - rel_pos) << 8) | slot;
 }
 
-template <int M, int T>
+// GRID: the cloud's P CTAs are co-resident but not one cluster; the lists go
+// through global memory (a.glist, by round parity) and a grid barrier (a.gbar)
+// replaces the cluster copies and mbarriers.
+template <int M, int T, bool GRID>
 __global__ void __launch_bounds__(kRoundThreads, 1)
 fps_rounds_cluster(const LoopArgs a) {
   constexpr int THREADS = kRoundThreads;
-  constexpr int W = kWarps;
   extern __shared__ float4 smem[];
   __shared__ RoundCtl<T> ctl;
 
@@ -586,7 +592,7 @@ fps_rounds_cluster(const LoopArgs a) {
         }
         // stage the list (after the previous round's copies have read it),
         // then copy it into every CTA's list[buf][crank]
-        if ((uint32_t)lane < P) bulk_wait_read_all();
+        if (!GRID && (uint32_t)lane < P) bulk_wait_read_all();
         __syncwarp();
 #pragma unroll
         for (int r = 0; r < G; ++r)
@@ -609,33 +615,59 @@ fps_rounds_cluster(const LoopArgs a) {
           ctl.stage.bound = bound;
           ctl.stage.pad = 0ull;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if ((uint32_t)lane < P) {
-          const uint32_t ra = mapa(smem_u32(&ctl.list[buf][crank]), lane);
-          const uint32_t rm = mapa(smem_u32(&ctl.mbar[buf]), lane);
-          bulk_copy_to_cluster(ra, smem_u32(&ctl.stage), (uint32_t)sizeof(CtaList<T>), rm);
-          bulk_commit();
-        }
-
-        // ---- wait for every CTA's list (bounded)
-        const uint32_t mb = smem_u32(&ctl.mbar[buf]);
-        const uint32_t parity = (round / kBufs) & 1u;
-        unsigned long long deadline = 0;
-        uint32_t polls = 0;
-        for (;;) {
-          const bool ok = mbar_try_wait(mb, parity, 20000u);
-          if (__all_sync(kFull, ok)) break;
-          if ((++polls & 255u) == 0) {
-            const unsigned long long now = globaltimer();
-            if (deadline == 0) deadline = now + (unsigned long long)tmo;
-            if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
+        if (!GRID) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if ((uint32_t)lane < P) {
+            const uint32_t ra = mapa(smem_u32(&ctl.list[buf][crank]), lane);
+            const uint32_t rm = mapa(smem_u32(&ctl.mbar[buf]), lane);
+            bulk_copy_to_cluster(ra, smem_u32(&ctl.stage), (uint32_t)sizeof(CtaList<T>), rm);
+            bulk_commit();
           }
+
+          // ---- wait for every CTA's list (bounded)
+          const uint32_t mb = smem_u32(&ctl.mbar[buf]);
+          const uint32_t parity = (round / kBufs) & 1u;
+          unsigned long long deadline = 0;
+          uint32_t polls = 0;
+          for (;;) {
+            const bool ok = mbar_try_wait(mb, parity, 20000u);
+            if (__all_sync(kFull, ok)) break;
+            if ((++polls & 255u) == 0) {
+              const unsigned long long now = globaltimer();
+              if (deadline == 0) deadline = now + (unsigned long long)tmo;
+              if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
+            }
+          }
+          if (lane == 0) mbar_arm(mb, tx_bytes);  // for round + kBufs
+        } else {
+          // ---- publish to global memory, then a grid barrier (bounded).  Slot
+          // (round & 1) is rewritten two rounds later, after every CTA passed
+          // the next barrier, so after every CTA read it.
+          __syncwarp();
+          constexpr int kWords = (int)(sizeof(CtaList<T>) / 16);
+          const uint4 *src = reinterpret_cast<const uint4 *>(&ctl.stage);
+          uint4 *dst = a.glist + ((size_t)(round & 1u) * P + crank) * kWords;
+          for (int w = lane; w < kWords; w += 32) __stcg(dst + w, src[w]);
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t target = (round + 1u) * P;
+            atomicAdd(a.gbar, 1u);
+            unsigned long long deadline = 0;
+            uint32_t polls = 0;
+            while (ld_acquire_gpu(a.gbar) < target) {
+              __nanosleep(64);
+              if ((++polls & 255u) == 0) {
+                const unsigned long long now = globaltimer();
+                if (deadline == 0) deadline = now + (unsigned long long)tmo;
+                if (now > deadline) { timed_out = true; break; }
+              }
+            }
+          }
+          timed_out = __shfl_sync(kFull, timed_out ? 1 : 0, 0) != 0;
         }
-        if (lane == 0) {
-          mbar_arm(mb, tx_bytes);  // for round + kBufs
-          ctl.timed_out = timed_out ? 1u : 0u;
-        }
+        if (lane == 0) ctl.timed_out = timed_out ? 1u : 0u;
       }
       // every list is in and the timeout flag is set
       if (kReplay > 1) replay_sync(); else __syncwarp();
@@ -646,12 +678,15 @@ fps_rounds_cluster(const LoopArgs a) {
       if (!finished) {
         const uint32_t pbase = a.poff[cloud];
         // B* = the largest bound, in the replay key's encoding
+        const CtaList<T> *lists =
+            GRID ? reinterpret_cast<const CtaList<T> *>(a.glist) + (size_t)(round & 1u) * P
+                 : ctl.list[buf];
         unsigned long long bl = 0ull;
-        if ((uint32_t)lane < P) {
-          bl = ctl.list[buf][lane].bound;
-          if (bl != 0ull)
-            bl = (bl & 0xffffffff00000000ull) |
-                 replay_lo((0xffffffffu - (uint32_t)bl) - pbase, 0u);
+        for (uint32_t i = (uint32_t)lane; i < P; i += 32u) {
+          unsigned long long b = GRID ? __ldcg(&lists[i].bound) : lists[i].bound;
+          if (b != 0ull)
+            b = (b & 0xffffffff00000000ull) | replay_lo((0xffffffffu - (uint32_t)b) - pbase, 0u);
+          bl = max64(bl, b);
         }
         const unsigned long long bstar = warp_max64_key(bl);
         // Only candidates that beat B* can be chosen this round (keys only
@@ -663,7 +698,7 @@ fps_rounds_cluster(const LoopArgs a) {
           const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
           lv[c] = false;
           if (idx < NC) {
-            const Cand &cd = ctl.list[buf][idx / T].c[idx % T];
+            const Cand cd = load_cand<GRID>(&lists[idx / T].c[idx % T]);
             lv[c] = cd.d >= 0.0f &&
                     (((unsigned long long)dkey(cd.d) << 32) | replay_lo(cd.pos - pbase, 0u)) > bstar;
           }
@@ -684,7 +719,7 @@ fps_rounds_cluster(const LoopArgs a) {
         for (int c = 0; c < kCandPerLane; ++c)
           if (lv[c]) {
             const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
-            ctl.live[off + lslot[c]] = ctl.list[buf][idx / T].c[idx % T];
+            ctl.live[off + lslot[c]] = load_cand<GRID>(&lists[idx / T].c[idx % T]);
           }
         if (kReplay > 1) replay_sync(); else __syncwarp();
         // live candidate i sits in lane i % 32 of warp (i / 32) % kReplay, row
@@ -901,13 +936,13 @@ fps_rounds_cluster(const LoopArgs a) {
   // remote write of that round was awaited, so no final cluster barrier.
 }
 
-template <int M, int T>
+template <int M, int T, bool GRID>
 cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
-  auto kern = fps_rounds_cluster<M, T>;
+  auto kern = fps_rounds_cluster<M, T, GRID>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err) return err;
-  if (a.P > 8) {
+  if (!GRID && a.P > 8) {
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (err) return err;
   }
@@ -917,29 +952,39 @@ cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.P;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  if (GRID) {  // every CTA co-resident (the grid barrier needs it), or no launch
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.P;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int T>
+template <int T, bool GRID>
 cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t st) {
   switch (m) {
-    case 1: return launch_rounds<1, T>(a, smem, st);
-    case 2: return launch_rounds<2, T>(a, smem, st);
-    case 3: return launch_rounds<3, T>(a, smem, st);
-    case 4: return launch_rounds<4, T>(a, smem, st);
-    case 6: return kMaxLeavesPerThread >= 6 ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T>(a, smem, st)
-                                            : cudaErrorInvalidValue;
-    case 8: return kMaxLeavesPerThread >= 8 ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T>(a, smem, st)
-                                            : cudaErrorInvalidValue;
+    case 1: return launch_rounds<1, T, GRID>(a, smem, st);
+    case 2: return launch_rounds<2, T, GRID>(a, smem, st);
+    case 3: return launch_rounds<3, T, GRID>(a, smem, st);
+    case 4: return launch_rounds<4, T, GRID>(a, smem, st);
+    case 6: return kMaxLeavesPerThread >= 6
+                       ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T, GRID>(a, smem, st)
+                       : cudaErrorInvalidValue;
+    case 8: return kMaxLeavesPerThread >= 8
+                       ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T, GRID>(a, smem, st)
+                       : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
+
+// Grid-wide rounds publish kGridT candidates per CTA (P * kGridT <= 256).
+constexpr int kGridT = 2;
 
 }  // namespace
 
@@ -962,14 +1007,30 @@ int rounds_max_smem(uint32_t P) {
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  (void)P;
-  return optin - (int)sizeof(RoundCtl<16>) - 1024;
+  // the grid-wide loop (P > one cluster) keeps smaller lists in shared memory
+  const int ctl = P > (uint32_t)kMaxClusterP ? (int)sizeof(RoundCtl<kGridT>) : (int)sizeof(RoundCtl<16>);
+  return optin - ctl - 1024;
 }
+
+int rounds_grid_candidates_per_cta(uint32_t P) {
+  return P * kGridT <= (uint32_t)kMaxCands ? kGridT : 0;
+}
+
+size_t rounds_grid_list_bytes(uint32_t P) { return 2 * (size_t)P * sizeof(CtaList<kGridT>); }
 
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                        uint32_t &launches) {
-  if (a.P > (uint32_t)kMaxClusterP || !plan.direct) return cudaErrorInvalidValue;
-  const cudaError_t err = launch_rounds_m<16>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+  if (!plan.direct) return cudaErrorInvalidValue;
+  cudaError_t err;
+  if (plan.mode == 1) {
+    if (a.B != 1 || !a.glist || !a.gbar || rounds_grid_candidates_per_cta(a.P) == 0)
+      return cudaErrorInvalidValue;
+    if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t), st))) return err;
+    err = launch_rounds_m<kGridT, true>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+  } else {
+    if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
+    err = launch_rounds_m<16, false>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+  }
   launches += 1;
   return err;
 }

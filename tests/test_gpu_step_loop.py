@@ -67,3 +67,18 @@ def test_step_loop_matches_round_loop(tmp_path):
         np.testing.assert_array_equal(rounds[name], steps[name], err_msg=name)
         if name == "c1":
             np.testing.assert_array_equal(rounds[name], oracle.fps(clouds[name], k, bounds, blocks))
+
+
+def test_grid_wide_round_loop_matches_oracle():
+    """A single cloud too large for one cluster's shared memory runs the
+    round loop over co-resident CTAs (lists through global memory)."""
+    import oracle
+    from tests import capi
+    pts = synthetic.cluster_cloud(n=400_000, seed=21, n_clusters=20)
+    bounds = (-100, 100, -100, 100, -100, 100)
+    blocks = (32, 32, 32)
+    capi.set_profiling(True)
+    got = capi.fps(pts, 3000, bounds, blocks)
+    assert capi.last_profile().mode == 3  # the grid-wide round loop ran
+    assert capi.last_profile().ctas_per_cloud > 16
+    np.testing.assert_array_equal(got, oracle.fps(pts, 3000, bounds, blocks))
