@@ -751,13 +751,14 @@ fps_rounds_cluster(const LoopArgs a) {
         // reference; the candidates' updates commute (min).
         uint32_t iter = 0;
         // the loop, with the cube source fixed (no branch on it per step)
-        auto replay = [&](auto use_regtab) {
+        auto replay = [&](auto use_regtab, auto nrows) {
           constexpr bool kRegTab = decltype(use_regtab)::value;
+          constexpr int R = decltype(nrows)::value;  // candidate rows in use
           for (;;) {
             unsigned long long kk[kCandPerLane];
 #pragma unroll
             for (int c = 0; c < kCandPerLane; ++c)
-              kk[c] = (uint32_t)c < rows ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
+              kk[c] = c < R ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
             unsigned long long wt[kSpec];  // this warp's best keys, in order
 #pragma unroll
             for (int j = 0; j < kSpec; ++j) {
@@ -857,7 +858,7 @@ fps_rounds_cluster(const LoopArgs a) {
             for (int j = 0; j < kSpec; ++j)
               if ((uint32_t)j < m) {
 #pragma unroll
-                for (int c = 0; c < kCandPerLane; ++c) {  // branch-free per candidate
+                for (int c = 0; c < R; ++c) {  // branch-free per candidate
                   const float d = sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]);
                   cdd[c] = (in_box(ccell[c], wcube[j][0], wcube[j][1], wcube[j][2]) && d < cdd[c])
                                ? d : cdd[c];
@@ -868,7 +869,19 @@ fps_rounds_cluster(const LoopArgs a) {
             if (it >= a.k || n >= (uint32_t)kQueue) break;
           }
         };
-        if (regtab) replay(std::true_type{}); else replay(std::false_type{});
+        // rows fixed per round: the steps touch only the rows in use
+        using std::integral_constant;
+        if (!regtab) {
+          replay(std::false_type{}, integral_constant<int, kCandPerLane>{});
+        } else if (rows <= 1) {
+          replay(std::true_type{}, integral_constant<int, 1>{});
+        } else if (rows == 2 || kCandPerLane == 2) {
+          replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 2 ? 2 : kCandPerLane)>{});
+        } else if (rows <= 4 || kCandPerLane == 4) {
+          replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 4 ? 4 : kCandPerLane)>{});
+        } else {
+          replay(std::true_type{}, integral_constant<int, kCandPerLane>{});
+        }
         if (it >= a.k) finished = true;
       }
       if (warp == 0 && lane == 0) {
