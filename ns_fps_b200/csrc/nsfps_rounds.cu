@@ -36,8 +36,8 @@
 //      apply the queued samples to their leaves, in order, as they appear
 //      (release/acquire on a shared counter).
 //
-// Buffers rotate over four rounds (a CTA publishes round r+1 only after it
-// has every round-r list), waits are bounded by %globaltimer.
+// Received lists rotate over two buffers (a CTA publishes round r+1 only
+// after it has every round-r list); waits are bounded by %globaltimer.
 #include <type_traits>
 
 #include "nsfps_device.cuh"
@@ -75,7 +75,18 @@ __device__ __forceinline__ int worker_index(int warp) {
   if (kIdle && warp >= 4 && warp < 4 + kIdle) return -1;
   return warp - kReplay - ((kIdle && warp >= 4 + kIdle) ? kIdle : 0);
 }
-constexpr int kMaxCands = 256;                          // P * T
+// Candidates each CTA of a cluster publishes per round (a build-time choice).
+#ifndef NSFPS_ROUND_T
+#define NSFPS_ROUND_T 12
+#endif
+constexpr int kRoundT = NSFPS_ROUND_T;
+constexpr int kMaxCands = kRoundT * 16 > 256 ? kRoundT * 16 : 256;  // P * T
+static_assert(kMaxCands <= 512, "at most 512 candidates (9-bit slots)");
+// Received lists rotate over two buffers: a CTA publishes round r+2 only
+// after it has every round r+1 list, so after every CTA compacted round r.
+constexpr int kListBufs = 2;
+// Bits of the candidate slot in a replay key.
+constexpr int kSlotBits = kMaxCands > 256 ? 9 : 8;
 constexpr int kCandPerLane = kMaxCands / (32 * kReplay);
 constexpr int kQueue = 512;                    // samples decided per round, at most
 constexpr int kBatch = 1;                      // samples a worker applies together
@@ -109,11 +120,11 @@ struct __align__(16) CtaList {
 
 template <int T>
 struct RoundCtl {
-  CtaList<T> list[kBufs][kMaxClusterP];  // received lists, by source CTA
+  CtaList<T> list[kListBufs][kMaxClusterP];  // received lists, by source CTA
   CtaList<T> stage;                      // this CTA's list, copied out from here
   Cand live[kMaxCands];                  // the round's candidates that beat B*
   uint32_t nlive[kReplay];
-  unsigned long long mbar[kBufs];
+  unsigned long long mbar[kListBufs];
   unsigned long long wkey[kWarps][T + 1];   // per-warp best leaves
   uint32_t wleaf[kWarps][T + 1];
   uint32_t mleaf[T + 1];                    // the CTA's T+1 best leaves
@@ -189,13 +200,14 @@ __device__ __forceinline__ void replay_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(32 * kReplay) : "memory");
 }
 
-// Replay keys: the distance key above ((0xffffff - cloud-relative sorted
-// position) << 8 | candidate slot).  Ordered like pkey() inside one cloud
-// (positions are unique, so the slot never decides), and the winner's slot
-// and position read straight out of the key.  A cloud part of one kernel has
-// fewer than 16 * 65536 points, so the position fits in 24 bits.
+// Replay keys: the distance key above ((2^(32-S) - 1 - cloud-relative sorted
+// position) << S | candidate slot), S = kSlotBits.  Ordered like pkey()
+// inside one cloud (positions are unique, so the slot never decides), and the
+// winner's slot and position read straight out of the key.  One cloud spans
+// at most 128 CTAs of fewer than 65536 points, so the position fits in
+// 32 - S >= 23 bits.
 __device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
-  return ((0xffffffu - rel_pos) << 8) | slot;
+  return ((((1u << (32 - kSlotBits)) - 1u) - rel_pos) << kSlotBits) | slot;
 }
 
 // GRID: the cloud's P CTAs are co-resident but not one cluster; the lists go
@@ -359,9 +371,9 @@ fps_rounds_cluster(const LoopArgs a) {
 
   const uint32_t tx_bytes = P * (uint32_t)sizeof(CtaList<T>);
   if (tid == 0) {
-    for (int b = 0; b < kBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
+    for (int b = 0; b < kListBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
     fence_mbar_init();
-    for (int b = 0; b < kBufs; ++b) mbar_arm(smem_u32(&ctl.mbar[b]), tx_bytes);
+    for (int b = 0; b < kListBufs; ++b) mbar_arm(smem_u32(&ctl.mbar[b]), tx_bytes);
     ctl.finished = 0;
   }
   __syncthreads();
@@ -473,7 +485,7 @@ fps_rounds_cluster(const LoopArgs a) {
 
   uint32_t out_n = 0, out_first = 0;  // the round's samples (worker warps)
   for (uint32_t round = 0;; ++round) {
-    const uint32_t buf = round & (kBufs - 1);
+    const uint32_t buf = round & (kListBufs - 1);
 
     // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum, in
     // order (keys are unique: every leaf has its own sorted position)
@@ -627,7 +639,7 @@ fps_rounds_cluster(const LoopArgs a) {
 
           // ---- wait for every CTA's list (bounded)
           const uint32_t mb = smem_u32(&ctl.mbar[buf]);
-          const uint32_t parity = (round / kBufs) & 1u;
+          const uint32_t parity = (round / kListBufs) & 1u;
           unsigned long long deadline = 0;
           uint32_t polls = 0;
           for (;;) {
@@ -639,7 +651,7 @@ fps_rounds_cluster(const LoopArgs a) {
               if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
             }
           }
-          if (lane == 0) mbar_arm(mb, tx_bytes);  // for round + kBufs
+          if (lane == 0) mbar_arm(mb, tx_bytes);  // for round + kListBufs
         } else {
           // ---- publish to global memory, then a grid barrier (bounded).  Slot
           // (round & 1) is rewritten two rounds later, after every CTA passed
@@ -805,7 +817,7 @@ fps_rounds_cluster(const LoopArgs a) {
             uint32_t wcell[kSpec], wcube[kSpec][3];
 #pragma unroll
             for (int j = 0; j < kSpec; ++j) {
-              const Cand &qcd = ctl.live[(uint32_t)wt[j] & 0xffu];
+              const Cand &qcd = ctl.live[(uint32_t)wt[j] & ((1u << kSlotBits) - 1u)];
               const float4 qv = *reinterpret_cast<const float4 *>(&qcd.x);
               wx[j] = qv.x; wy[j] = qv.y; wz[j] = qv.z;
               wcell[j] = qcd.cell;
@@ -849,7 +861,7 @@ fps_rounds_cluster(const LoopArgs a) {
                   Sample sm;
                   sm.q = make_float4(wx[j], wy[j], wz[j], wd[j]);
                   sm.c = make_uint4(wcube[j][0], wcube[j][1], wcube[j][2],
-                                    pbase + (0xffffffu - ((uint32_t)wt[j] >> 8)));
+                                    pbase + (((1u << (32 - kSlotBits)) - 1u) - ((uint32_t)wt[j] >> kSlotBits)));
                   s_samp[n + j] = sm;
                 }
               st_release_cta_if(lane == 0, &ctl.produced, n + m);  // the workers may apply them
@@ -1001,7 +1013,7 @@ constexpr int kGridT = 2;
 
 }  // namespace
 
-int rounds_candidates_per_cta(uint32_t) { return 16; }
+int rounds_candidates_per_cta(uint32_t) { return kRoundT; }
 
 int rounds_leaves_per_thread(uint32_t leaves) {
   static const int ms[] = {1, 2, 3, 4, 6, 8};
@@ -1021,7 +1033,7 @@ int rounds_max_smem(uint32_t P) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   // the grid-wide loop (P > one cluster) keeps smaller lists in shared memory
-  const int ctl = P > (uint32_t)kMaxClusterP ? (int)sizeof(RoundCtl<kGridT>) : (int)sizeof(RoundCtl<16>);
+  const int ctl = P > (uint32_t)kMaxClusterP ? (int)sizeof(RoundCtl<kGridT>) : (int)sizeof(RoundCtl<kRoundT>);
   return optin - ctl - 1024;
 }
 
@@ -1042,7 +1054,7 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
     err = launch_rounds_m<kGridT, true>(a, plan.leaves_per_thread, plan.smem_bytes, st);
   } else {
     if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
-    err = launch_rounds_m<16, false>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+    err = launch_rounds_m<kRoundT, false>(a, plan.leaves_per_thread, plan.smem_bytes, st);
   }
   launches += 1;
   return err;
