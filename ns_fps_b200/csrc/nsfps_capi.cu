@@ -465,8 +465,10 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   NSFPS_CUDA(cudaStreamSynchronize(st));
 
   // CTAs per cloud: the smallest count whose largest part fits in shared
-  // memory; then, while every cloud still gets its own SMs, keep doubling it
-  // until each thread owns a single leaf (less serial work per iteration).
+  // memory; then, while every cloud still gets its own SMs, keep doubling it:
+  // for the round loop up to the cluster limit (fewer leaves per worker warp,
+  // the same steps), for the per-step loop until each thread owns a single
+  // leaf (more CTAs also mean more proposals per step there).
   const int max_smem = loop_max_smem();
   uint32_t max_tab = 0;
   for (const RangeDev &r : j.ranges)
@@ -498,7 +500,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
         pi = i; m_sel = m; bytes_sel = bytes;
         continue;
       }
-      if (m_sel == 1 || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
+      if ((!rounds && m_sel == 1) || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
       pi = i; m_sel = m; bytes_sel = bytes;
     }
   };
