@@ -288,6 +288,9 @@ constexpr uint32_t kClusterCand[] = {1, 2, 4, 8, 16, 32, 64, 128};
 constexpr int kNumCand = 8;
 constexpr int kNumCluster = 5;
 constexpr uint32_t kMaxGridP = 128;
+// Points from which one cloud runs on the grid-wide loop even when it fits a
+// cluster.
+constexpr uint32_t kGridMinPoints = NSFPS_GRID_MIN_POINTS;
 
 size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   const size_t n = j.n;
@@ -322,7 +325,8 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   b.out_count = c.take<uint32_t>(j.B);
   b.out = own_out ? c.take<uint64_t>((size_t)j.B * j.k) : nullptr;
   b.stats = c.take<unsigned long long>(4);
-  b.glist = j.B == 1 ? c.take<uint4>(rounds_grid_list_bytes(kMaxGridP) / 16) : nullptr;
+  b.glist = j.B == 1 ? c.take<uint4>(std::max(rounds_grid_list_bytes(64), rounds_grid_list_bytes(128)) / 16)
+                     : nullptr;
   b.gbar = j.B == 1 ? c.take<uint32_t>(1) : nullptr;
   return align_up(c.off, 256);
 }
@@ -511,19 +515,26 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   }
   // one cloud too large for a cluster: the grid-wide round loop over P
   // co-resident CTAs (one per SM), the smallest P that fits
+  // A single cloud too large for a cluster takes the grid-wide round loop
+  // over P co-resident CTAs (one per SM), the smallest P that fits.  So does
+  // a single cloud of many points that fits a cluster: over more CTAs its
+  // parts are smaller (lighter workers, shorter lists) and it runs faster.
   bool grid = false;
-  if (pi < 0 && j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist) {
-    rounds = true;
-    for (int i = kNumCluster; i < kNumCand && pi < 0; ++i) {
+  if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&
+      (pi < 0 || j.n >= kGridMinPoints)) {
+    for (int i = kNumCluster; i < kNumCand && !grid; ++i) {
       const uint32_t P = kClusterCand[i];
       if (P > (uint32_t)sms || P > kMaxGridP || rounds_grid_candidates_per_cta(P) == 0) continue;
+      const bool was_rounds = rounds;
+      rounds = true;
       int m;
       size_t bytes;
       if (fits(i, m, bytes)) {
         pi = i; m_sel = m; bytes_sel = bytes; grid = true;
+      } else {
+        rounds = was_rounds;
       }
     }
-    if (!grid) rounds = !j.any_hashed && !g_force_steps.load();
   }
   if (pi < 0)
     return set_error(NSFPS_ERR_UNSUPPORTED,

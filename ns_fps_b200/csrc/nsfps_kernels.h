@@ -21,6 +21,11 @@ constexpr uint32_t kStatusBadPlan = 2u;
 
 constexpr int kMaxCand = 8;
 
+// Points from which a single cloud takes the grid-wide round loop (build-time).
+#ifndef NSFPS_GRID_MIN_POINTS
+#define NSFPS_GRID_MIN_POINTS 98304u
+#endif
+
 // Threads per CTA of the sampling loop; a thread owns up to 8 leaves
 // (template instances 1, 2, 3, 4, 6, 8).  Must be a multiple of 32, at most
 // 512 (a build-time choice: -DNSFPS_LOOP_THREADS=...).

@@ -1008,8 +1008,9 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
   }
 }
 
-// Grid-wide rounds publish kGridT candidates per CTA (P * kGridT <= 256).
-constexpr int kGridT = 2;
+// Grid-wide rounds over P = 64 or 128 CTAs publish 256 / P candidates per
+// CTA (256 in all, as a full cluster does).
+constexpr int grid_t(uint32_t P) { return P == 64u ? 4 : (P == 128u ? 2 : 0); }
 
 }  // namespace
 
@@ -1033,15 +1034,20 @@ int rounds_max_smem(uint32_t P) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   // the grid-wide loop (P > one cluster) keeps smaller lists in shared memory
-  const int ctl = P > (uint32_t)kMaxClusterP ? (int)sizeof(RoundCtl<kGridT>) : (int)sizeof(RoundCtl<kRoundT>);
+  const int ctl = P == 64u    ? (int)sizeof(RoundCtl<grid_t(64)>)
+                  : P == 128u ? (int)sizeof(RoundCtl<grid_t(128)>)
+                              : (int)sizeof(RoundCtl<kRoundT>);
   return optin - ctl - 1024;
 }
 
 int rounds_grid_candidates_per_cta(uint32_t P) {
-  return P * kGridT <= (uint32_t)kMaxCands ? kGridT : 0;
+  return grid_t(P);
 }
 
-size_t rounds_grid_list_bytes(uint32_t P) { return 2 * (size_t)P * sizeof(CtaList<kGridT>); }
+size_t rounds_grid_list_bytes(uint32_t P) {
+  return P == 64u ? 2 * (size_t)P * sizeof(CtaList<grid_t(64)>)
+                  : (P == 128u ? 2 * (size_t)P * sizeof(CtaList<grid_t(128)>) : 0);
+}
 
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                        uint32_t &launches) {
@@ -1051,7 +1057,8 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
     if (a.B != 1 || !a.glist || !a.gbar || rounds_grid_candidates_per_cta(a.P) == 0)
       return cudaErrorInvalidValue;
     if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t), st))) return err;
-    err = launch_rounds_m<kGridT, true>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+    err = a.P == 64u ? launch_rounds_m<grid_t(64), true>(a, plan.leaves_per_thread, plan.smem_bytes, st)
+                     : launch_rounds_m<grid_t(128), true>(a, plan.leaves_per_thread, plan.smem_bytes, st);
   } else {
     if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
     err = launch_rounds_m<kRoundT, false>(a, plan.leaves_per_thread, plan.smem_bytes, st);
