@@ -145,7 +145,9 @@ NSFPS_API int nsfps_fps_batched(const float *const *clouds, const uint64_t *n,
 /* Device-resident sampling for callers that keep clouds in HBM: `count`
  * clouds packed back to back in d_xyz (offsets[i]..offsets[i+1] points,
  * offsets in HOST memory, count + 1 entries), ranges as in
- * nsfps_fps_batched (host memory, non-NULL), d_out a DEVICE buffer of
+ * nsfps_fps_batched (host memory; NULL selects compute_bbox(cloud, 16, 16,
+ * 16) per cloud, like fps(range=None), with the min/max reduction done on the
+ * device, src/yuezu_fps.cpp:643-670), d_out a DEVICE buffer of
  * count * k uint64 (cloud i at d_out + i * k), out_len a HOST array of
  * `count` lengths.  Work is issued on `stream` (a cudaStream_t; NULL = the
  * legacy default stream) of the current device; the call returns after the

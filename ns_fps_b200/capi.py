@@ -122,10 +122,13 @@ def fps_device(d_xyz_ptr: int, offsets, k: int, ranges, per_cloud: bool, d_out_p
     """nsfps_fps_device: clouds already in device memory (packed float32 xyz at
     d_xyz_ptr, `offsets` = count + 1 point offsets), results to the device
     buffer at d_out_ptr (count * k uint64).  `ranges` is one (bounds, blocks)
-    pair or a list of them.  Returns the per-cloud sample counts."""
+    pair, a list of them, or None (each cloud's bounding box with 16^3
+    blocks, computed on the device).  Returns the per-cloud sample counts."""
     count = len(offsets) - 1
     offs = (ctypes.c_uint64 * (count + 1))(*[int(o) for o in offsets])
-    if per_cloud:
+    if ranges is None:  # compute_bbox(cloud, 16, 16, 16) per cloud, on the device
+        rs = None
+    elif per_cloud:
         rs = (Range * count)(*[rng(b, bl) for b, bl in ranges])
     else:
         rs = (Range * 1)(rng(*ranges))

@@ -647,6 +647,45 @@ nsfps_range bbox_of(const float *xyz, uint64_t n, uint32_t xb, uint32_t yb, uint
   return r;
 }
 
+// compute_bbox(cloud, 16, 16, 16) of `count` device-resident clouds (the
+// reference's fps(range=None) path, src/yuezu_fps.cpp:643-670), with the
+// reduction on the device and the same float arithmetic as bbox_of after it.
+int device_bboxes(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz, const uint64_t *offsets,
+                  uint64_t count, std::vector<nsfps_range> &rs) {
+  const size_t off_bytes = align_up(sizeof(uint32_t) * (count + 1), 256);
+  int rc = ensure_ws(ctx, off_bytes + sizeof(float) * 6 * count);
+  if (rc) return rc;
+  uint32_t *d_poff = (uint32_t *)ctx->ws;
+  float *d_box = (float *)((char *)ctx->ws + off_bytes);
+  std::vector<uint32_t> hpoff(count + 1);
+  for (uint64_t i = 0; i <= count; ++i) {
+    if (offsets[i] - offsets[0] >= (1ull << 31))
+      return set_error(NSFPS_ERR_UNSUPPORTED, "too many points in one call");
+    hpoff[i] = (uint32_t)(offsets[i] - offsets[0]);
+  }
+  std::vector<float> hbox(6 * count);
+  uint32_t launches = 0;
+  NSFPS_CUDA(cudaMemcpyAsync(d_poff, hpoff.data(), sizeof(uint32_t) * (count + 1),
+                             cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(run_cloud_bbox(d_xyz, d_poff, (uint32_t)count, d_box, st, launches));
+  NSFPS_CUDA(cudaMemcpyAsync(hbox.data(), d_box, sizeof(float) * 6 * count,
+                             cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaStreamSynchronize(st));
+  const float eps = NSFPS_BOUNDARY_EPS;
+  rs.resize(count);
+  for (uint64_t c = 0; c < count; ++c) {
+    const float *b = &hbox[6 * c];
+    nsfps_range &r = rs[c];
+    r.min_x = b[0] - eps; r.max_x = b[3] + eps;
+    r.min_y = b[1] - eps; r.max_y = b[4] + eps;
+    r.min_z = b[2] - eps; r.max_z = b[5] + eps;
+    r.x_blocks = NSFPS_DEFAULT_X_BLOCKS;
+    r.y_blocks = NSFPS_DEFAULT_Y_BLOCKS;
+    r.z_blocks = NSFPS_DEFAULT_Z_BLOCKS;
+  }
+  return NSFPS_OK;
+}
+
 // Clouds handled without the GPU, exactly as yuezu_fps's early returns
 // (src/yuezu_fps.cpp:678-688): n == 0 or k == 0 -> [], k >= n -> 0..n-1.
 bool trivial(uint64_t n, uint64_t k) { return n == 0 || k == 0 || k >= n; }
@@ -909,7 +948,7 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
                      uint64_t *d_out, uint64_t *out_len, void *stream) {
   clear_error();
   if (count == 0) return NSFPS_OK;
-  if (!offsets || !ranges || !out_len || !d_out)
+  if (!offsets || !out_len || !d_out || !d_xyz)
     return set_error(NSFPS_ERR_ARG, "NULL argument");
   int dev = 0;
   NSFPS_CUDA(cudaGetDevice(&dev));
@@ -923,14 +962,6 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
     if (offsets[i + 1] < offsets[i]) return set_error(NSFPS_ERR_ARG, "offsets must not decrease");
     n[i] = offsets[i + 1] - offsets[i];
   }
-  std::vector<nsfps_range> rs;
-  std::vector<uint32_t> rid(count, 0);
-  if (per_cloud_ranges) {
-    rs.assign(ranges, ranges + count);
-    for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
-  } else {
-    rs.push_back(ranges[0]);
-  }
   // clouds needing no sampling loop are answered here; the others run as one job
   bool all_gpu = true;
   for (uint64_t i = 0; i < count; ++i) if (trivial(n[i], k)) all_gpu = false;
@@ -938,6 +969,18 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
     return set_error(NSFPS_ERR_UNSUPPORTED,
                      "nsfps_fps_device needs 0 < k < n for every cloud");
   if (offsets[0] != 0) d_xyz += 3 * offsets[0];
+  std::vector<nsfps_range> rs;
+  std::vector<uint32_t> rid(count, 0);
+  if (!ranges) {
+    rc = device_bboxes(ctx, user, d_xyz, offsets, count, rs);
+    if (rc) return rc;
+    for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
+  } else if (per_cloud_ranges) {
+    rs.assign(ranges, ranges + count);
+    for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
+  } else {
+    rs.push_back(ranges[0]);
+  }
   Job j;
   rc = build_job(n.data(), count, k, rs, rid, j);
   if (rc) return rc;

@@ -63,6 +63,11 @@ struct SetupArgs {
 
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches);
 
+// compute_bbox of each of B device-resident clouds (poff: B + 1 point
+// offsets, device): out[6c .. 6c+5] = min x, y, z, max x, y, z.
+cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, float *out,
+                           cudaStream_t st, uint32_t &launches);
+
 struct LoopArgs {
   uint32_t B;                 // clouds in this launch
   uint32_t k;                 // samples per cloud

@@ -397,11 +397,76 @@ __global__ void plan_partition(const float4 *__restrict__ leaf_lo,
   }
 }
 
+// compute_bbox (src/yuezu_fps.cpp:648-670) of each cloud, on the device: the
+// per-axis minimum and maximum of the cloud's points.  The reference scans
+// from point 0 with `v < min` / `max < v`, which never take a NaN, so a NaN
+// survives only as point 0's own coordinate; fminf/fmaxf skip NaNs the same
+// way elsewhere.  (Signed zeros can differ in which zero wins, which the
+// +-BOUNDARY_EPS applied afterwards makes irrelevant.)  One block per cloud.
+__global__ void __launch_bounds__(256)
+cloud_bbox(const float *__restrict__ xyz, const uint32_t *__restrict__ poff, uint32_t B,
+           float *__restrict__ out) {
+  const uint32_t c = blockIdx.x;
+  if (c >= B) return;
+  const uint32_t s = poff[c], e = poff[c + 1];
+  const float inf = __int_as_float(0x7f800000);
+  float mn[3] = {inf, inf, inf}, mx[3] = {-inf, -inf, -inf};
+  for (uint32_t i = s + threadIdx.x; i < e; i += blockDim.x) {
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      const float v = xyz[3 * (size_t)i + a];
+      mn[a] = fminf(mn[a], v);
+      mx[a] = fmaxf(mx[a], v);
+    }
+  }
+  __shared__ float red[6][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mn[a] = fminf(mn[a], __shfl_xor_sync(0xffffffffu, mn[a], o));
+      mx[a] = fmaxf(mx[a], __shfl_xor_sync(0xffffffffu, mx[a], o));
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int a = 0; a < 3; ++a) { red[a][warp] = mn[a]; red[3 + a][warp] = mx[a]; }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = (int)(blockDim.x >> 5);
+    for (int w = 1; w < nw; ++w)
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        red[a][0] = fminf(red[a][0], red[a][w]);
+        red[3 + a][0] = fmaxf(red[3 + a][0], red[3 + a][w]);
+      }
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      float lo = red[a][0], hi = red[3 + a][0];
+      if (e > s) {  // point 0 starts the scan: a NaN there is kept
+        const float v0 = xyz[3 * (size_t)s + a];
+        if (v0 != v0) lo = hi = v0;
+      }
+      out[6 * (size_t)c + a] = lo;
+      out[6 * (size_t)c + 3 + a] = hi;
+    }
+  }
+}
+
 inline uint32_t cdiv(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
 
 }  // namespace
 
 // ------------------------------------------------------------------ driver
+cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, float *out,
+                           cudaStream_t st, uint32_t &launches) {
+  if (B == 0) return cudaSuccess;
+  cloud_bbox<<<B, 256, 0, st>>>(xyz, poff, B, out);
+  launches += 1;
+  return cudaGetLastError();
+}
+
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
   const uint32_t n = a.n;
   const uint32_t B = a.B;
