@@ -299,7 +299,6 @@ fps_rounds_cluster(const LoopArgs a) {
   // (entries lane and lane + 32): the cube half-width n_a is the number of
   // thresholds below D (they increase with n), one ballot per 32 entries.
   const bool regtab = fast && n0 <= 64u && n1 <= 64u && n2 <= 64u;
-  const bool wide = n0 > 32u || n1 > 32u || n2 > 32u;
   float rt[3][2];
 #pragma unroll
   for (int d = 0; d < 3; ++d) {
@@ -736,20 +735,26 @@ fps_rounds_cluster(const LoopArgs a) {
         if (kReplay > 1) replay_sync(); else __syncwarp();
         // live candidate i sits in lane i % 32 of warp (i / 32) % kReplay, row
         // i / (32 * kReplay); rows past L are empty on every warp
-        float cx[kCandPerLane], cy[kCandPerLane], cz[kCandPerLane], cdd[kCandPerLane];
-        uint32_t clo[kCandPerLane], ccell[kCandPerLane];
+        // per candidate: coordinates, its distance as a key (dkey: for the
+        // non-negative distances here, integer order is float order, so
+        // min(old, d) is an integer min), the low key word, its cell split
+        // into axes (no candidate: key 0, cell outside every cube)
+        float cx[kCandPerLane], cy[kCandPerLane], cz[kCandPerLane];
+        uint32_t ck[kCandPerLane], clo[kCandPerLane];
+        uint32_t gx[kCandPerLane], gy[kCandPerLane], gz[kCandPerLane];
 #pragma unroll
         for (int c = 0; c < kCandPerLane; ++c) {
           const uint32_t idx = (uint32_t)(32 * kReplay * c + 32 * warp + lane);
           cx[c] = cy[c] = cz[c] = 0.0f;
-          cdd[c] = -1.0f;
-          clo[c] = 0u;  // no candidate: key 0
-          ccell[c] = 0xffffffffu;
+          ck[c] = 0u;
+          clo[c] = 0u;
+          gx[c] = gy[c] = gz[c] = 0xffffu;
           if (idx < L) {
             const Cand cd = ctl.live[idx];
-            cx[c] = cd.x; cy[c] = cd.y; cz[c] = cd.z; cdd[c] = cd.d;
+            cx[c] = cd.x; cy[c] = cd.y; cz[c] = cd.z;
+            ck[c] = dkey(cd.d);
             clo[c] = replay_lo(cd.pos - pbase, idx);
-            ccell[c] = cd.cell;
+            gx[c] = cd.cell & 1023u; gy[c] = (cd.cell >> 10) & 1023u; gz[c] = cd.cell >> 20;
           }
         }
         const uint32_t rows = (L + 32u * kReplay - 1u) / (32u * kReplay);
@@ -767,19 +772,40 @@ fps_rounds_cluster(const LoopArgs a) {
           constexpr bool kRegTab = decltype(use_regtab)::value;
           constexpr int R = decltype(nrows)::value;  // candidate rows in use
           for (;;) {
-            unsigned long long kk[kCandPerLane];
-#pragma unroll
-            for (int c = 0; c < kCandPerLane; ++c)
-              kk[c] = c < R ? (((unsigned long long)dkey(cdd[c]) << 32) | clo[c]) : 0ull;
             unsigned long long wt[kSpec];  // this warp's best keys, in order
+            if (kSpec == 1) {
+              // the largest distance key, then among its holders the largest
+              // low word: two 32-bit trees around the two warp reductions
+              uint32_t th[R];
 #pragma unroll
-            for (int j = 0; j < kSpec; ++j) {
-              unsigned long long tk[kCandPerLane];
+              for (int c = 0; c < R; ++c) th[c] = ck[c];
 #pragma unroll
-              for (int c = 0; c < kCandPerLane; ++c) tk[c] = kk[c];
-              wt[j] = warp_max64_key(tree_max64(tk));
+              for (int st = 1; st < R; st <<= 1)
 #pragma unroll
-              for (int c = 0; c < kCandPerLane; ++c) kk[c] = kk[c] == wt[j] ? 0ull : kk[c];
+                for (int c = 0; c + st < R; c += 2 * st) th[c] = max(th[c], th[c + st]);
+              const uint32_t mh = __reduce_max_sync(kFull, th[0]);
+              uint32_t tl[R];
+#pragma unroll
+              for (int c = 0; c < R; ++c) tl[c] = ck[c] == mh ? clo[c] : 0u;
+#pragma unroll
+              for (int st = 1; st < R; st <<= 1)
+#pragma unroll
+                for (int c = 0; c + st < R; c += 2 * st) tl[c] = max(tl[c], tl[c + st]);
+              wt[0] = ((unsigned long long)mh << 32) | __reduce_max_sync(kFull, tl[0]);
+            } else {
+              unsigned long long kk[kCandPerLane];
+#pragma unroll
+              for (int c = 0; c < kCandPerLane; ++c)
+                kk[c] = c < R ? (((unsigned long long)ck[c] << 32) | clo[c]) : 0ull;
+#pragma unroll
+              for (int j = 0; j < kSpec; ++j) {
+                unsigned long long tk[kCandPerLane];
+#pragma unroll
+                for (int c = 0; c < kCandPerLane; ++c) tk[c] = kk[c];
+                wt[j] = warp_max64_key(tree_max64(tk));
+#pragma unroll
+                for (int c = 0; c < kCandPerLane; ++c) kk[c] = kk[c] == wt[j] ? 0ull : kk[c];
+              }
             }
             if (kReplay > 1) {  // the best over the replay warps
               const uint32_t par = iter & 1u;
@@ -809,8 +835,13 @@ fps_rounds_cluster(const LoopArgs a) {
               wd[j] = __uint_as_float((uint32_t)(wt[j] >> 32) - 1u);  // current distance
             // stop when some unlisted point may win (not certain), or when the
             // best distance is 0 (src/yuezu_fps.cpp:705-706)
-            if (!(wt[0] > bstar && wd[0] > 0.0f)) {
-              finished = wt[0] > bstar;
+            // one exit test per step: k samples taken, the queue full, some
+            // unlisted point may win (not certain), or the best distance is 0
+            // (src/yuezu_fps.cpp:705-706); only the first and the last end
+            // the sampling
+            const bool more = it < a.k && n < (uint32_t)kQueue;
+            if (!(more && wt[0] > bstar && wd[0] > 0.0f)) {
+              finished = it >= a.k || (more && wt[0] > bstar);
               break;
             }
             float wx[kSpec], wy[kSpec], wz[kSpec];
@@ -831,7 +862,8 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
                 for (int d = 0; d < 3; ++d) {
                   int nh = __popc(__ballot_sync(kFull, qd > rt[d][0]));
-                  if (wide) nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
+                  // entries 32..63 (+inf where absent: no branch on the axis size)
+                  nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
                   const int top = ax[d].blocks - 1;
                   const int l = (int)qc[d] - nh > 0 ? (int)qc[d] - nh : 0;
                   const int h = (int)qc[d] + nh < top ? (int)qc[d] + nh : top;
@@ -854,7 +886,7 @@ fps_rounds_cluster(const LoopArgs a) {
                      !in_box(wcell[j], wcube[i][0], wcube[i][1], wcube[i][2]);
               m += ok ? 1u : 0u;
             }
-            if (warp == 0) {  // queue the samples (every lane stores the same values)
+            {  // queue the samples (every lane of every replay warp stores the same values)
 #pragma unroll
               for (int j = 0; j < kSpec; ++j)
                 if ((uint32_t)j < m) {
@@ -864,21 +896,22 @@ fps_rounds_cluster(const LoopArgs a) {
                                     pbase + (((1u << (32 - kSlotBits)) - 1u) - ((uint32_t)wt[j] >> kSlotBits)));
                   s_samp[n + j] = sm;
                 }
-              st_release_cta_if(lane == 0, &ctl.produced, n + m);  // the workers may apply them
+              st_release_cta_if(warp == 0 && lane == 0, &ctl.produced, n + m);  // workers may apply them
             }
 #pragma unroll
             for (int j = 0; j < kSpec; ++j)
               if ((uint32_t)j < m) {
 #pragma unroll
                 for (int c = 0; c < R; ++c) {  // branch-free per candidate
-                  const float d = sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]);
-                  cdd[c] = (in_box(ccell[c], wcube[j][0], wcube[j][1], wcube[j][2]) && d < cdd[c])
-                               ? d : cdd[c];
+                  const uint32_t dk = dkey(sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]));
+                  const bool in = (gx[c] - (wcube[j][0] & 0xffffu)) <= (wcube[j][0] >> 16) &&
+                                  (gy[c] - (wcube[j][1] & 0xffffu)) <= (wcube[j][1] >> 16) &&
+                                  (gz[c] - (wcube[j][2] & 0xffffu)) <= (wcube[j][2] >> 16);
+                  ck[c] = in ? min(ck[c], dk) : ck[c];
                 }
               }
             n += m;
             it += m;
-            if (it >= a.k || n >= (uint32_t)kQueue) break;
           }
         };
         // rows fixed per round: the steps touch only the rows in use
