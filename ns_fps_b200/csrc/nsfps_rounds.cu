@@ -768,8 +768,9 @@ fps_rounds_cluster(const LoopArgs a) {
         // reference; the candidates' updates commute (min).
         uint32_t iter = 0;
         // the loop, with the cube source fixed (no branch on it per step)
-        auto replay = [&](auto use_regtab, auto nrows) {
+        auto replay = [&](auto use_regtab, auto nrows, auto wide_axes) {
           constexpr bool kRegTab = decltype(use_regtab)::value;
+          constexpr bool kWide = decltype(wide_axes)::value;  // an axis has > 32 thresholds
           constexpr int R = decltype(nrows)::value;  // candidate rows in use
           for (;;) {
             unsigned long long wt[kSpec];  // this warp's best keys, in order
@@ -862,8 +863,7 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
                 for (int d = 0; d < 3; ++d) {
                   int nh = __popc(__ballot_sync(kFull, qd > rt[d][0]));
-                  // entries 32..63 (+inf where absent: no branch on the axis size)
-                  nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));
+                  if (kWide) nh += __popc(__ballot_sync(kFull, qd > rt[d][1]));  // entries 32..63
                   const int top = ax[d].blocks - 1;
                   const int l = (int)qc[d] - nh > 0 ? (int)qc[d] - nh : 0;
                   const int h = (int)qc[d] + nh < top ? (int)qc[d] + nh : top;
@@ -914,19 +914,26 @@ fps_rounds_cluster(const LoopArgs a) {
             it += m;
           }
         };
-        // rows fixed per round: the steps touch only the rows in use
+        // rows (and whether an axis has more than 32 thresholds) fixed per
+        // round: the steps touch only the rows in use, with no branch on them
         using std::integral_constant;
-        if (!regtab) {
-          replay(std::false_type{}, integral_constant<int, kCandPerLane>{});
-        } else if (rows <= 1) {
-          replay(std::true_type{}, integral_constant<int, 1>{});
-        } else if (rows == 2 || kCandPerLane == 2) {
-          replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 2 ? 2 : kCandPerLane)>{});
-        } else if (rows <= 4 || kCandPerLane == 4) {
-          replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 4 ? 4 : kCandPerLane)>{});
-        } else {
-          replay(std::true_type{}, integral_constant<int, kCandPerLane>{});
-        }
+        const bool wide = n0 > 32u || n1 > 32u || n2 > 32u;
+        auto replay_rows = [&](auto wide_axes) {
+          if (!regtab) {
+            replay(std::false_type{}, integral_constant<int, kCandPerLane>{}, wide_axes);
+          } else if (rows <= 1) {
+            replay(std::true_type{}, integral_constant<int, 1>{}, wide_axes);
+          } else if (rows == 2 || kCandPerLane == 2) {
+            replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 2 ? 2 : kCandPerLane)>{},
+                   wide_axes);
+          } else if (rows <= 4 || kCandPerLane == 4) {
+            replay(std::true_type{}, integral_constant<int, (kCandPerLane >= 4 ? 4 : kCandPerLane)>{},
+                   wide_axes);
+          } else {
+            replay(std::true_type{}, integral_constant<int, kCandPerLane>{}, wide_axes);
+          }
+        };
+        if (wide) replay_rows(std::true_type{}); else replay_rows(std::false_type{});
         if (it >= a.k) finished = true;
       }
       if (warp == 0 && lane == 0) {
