@@ -668,7 +668,7 @@ fps_rounds_cluster(const LoopArgs a) {
             unsigned long long deadline = 0;
             uint32_t polls = 0;
             while (ld_acquire_gpu(a.gbar) < target) {
-              __nanosleep(64);
+              if (polls >= 64u) __nanosleep(64);  // the first polls without backoff
               if ((++polls & 255u) == 0) {
                 const unsigned long long now = globaltimer();
                 if (deadline == 0) deadline = now + (unsigned long long)tmo;
@@ -692,6 +692,15 @@ fps_rounds_cluster(const LoopArgs a) {
         const CtaList<T> *lists =
             GRID ? reinterpret_cast<const CtaList<T> *>(a.glist) + (size_t)(round & 1u) * P
                  : ctl.list[buf];
+        // this lane's candidates, loaded together with the bounds (one
+        // round trip to L2 in the grid-wide loop)
+        Cand lc[kCandPerLane];
+#pragma unroll
+        for (int c = 0; c < kCandPerLane; ++c) {
+          const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
+          lc[c].d = -1.0f;
+          if (idx < NC) lc[c] = load_cand<GRID>(&lists[idx / T].c[idx % T]);
+        }
         unsigned long long bl = 0ull;
         for (uint32_t i = (uint32_t)lane; i < P; i += 32u) {
           unsigned long long b = GRID ? __ldcg(&lists[i].bound) : lists[i].bound;
@@ -706,13 +715,8 @@ fps_rounds_cluster(const LoopArgs a) {
         bool lv[kCandPerLane];
 #pragma unroll
         for (int c = 0; c < kCandPerLane; ++c) {
-          const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
-          lv[c] = false;
-          if (idx < NC) {
-            const Cand cd = load_cand<GRID>(&lists[idx / T].c[idx % T]);
-            lv[c] = cd.d >= 0.0f &&
-                    (((unsigned long long)dkey(cd.d) << 32) | replay_lo(cd.pos - pbase, 0u)) > bstar;
-          }
+          lv[c] = lc[c].d >= 0.0f &&
+                  (((unsigned long long)dkey(lc[c].d) << 32) | replay_lo(lc[c].pos - pbase, 0u)) > bstar;
           const uint32_t bm = __ballot_sync(kFull, lv[c]);
           lslot[c] = nl_w + __popc(bm & lanemask_lt());
           nl_w += __popc(bm);
@@ -728,10 +732,7 @@ fps_rounds_cluster(const LoopArgs a) {
         }
 #pragma unroll
         for (int c = 0; c < kCandPerLane; ++c)
-          if (lv[c]) {
-            const uint32_t idx = (uint32_t)(warp * 32 * kCandPerLane + 32 * c + lane);
-            ctl.live[off + lslot[c]] = load_cand<GRID>(&lists[idx / T].c[idx % T]);
-          }
+          if (lv[c]) ctl.live[off + lslot[c]] = lc[c];
         if (kReplay > 1) replay_sync(); else __syncwarp();
         // live candidate i sits in lane i % 32 of warp (i / 32) % kReplay, row
         // i / (32 * kReplay); rows past L are empty on every warp
