@@ -77,7 +77,7 @@ __device__ __forceinline__ int worker_index(int warp) {
 }
 // Candidates each CTA of a cluster publishes per round (a build-time choice).
 #ifndef NSFPS_ROUND_T
-#define NSFPS_ROUND_T 12
+#define NSFPS_ROUND_T 8
 #endif
 constexpr int kRoundT = NSFPS_ROUND_T;
 constexpr int kMaxCands = kRoundT * 16 > 256 ? kRoundT * 16 : 256;  // P * T
