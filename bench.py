@@ -321,7 +321,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": peak_kind,
-                         "kernel": "fps_rounds_cluster" if loop_mode == 2 else "fps_loop_cluster",
+                         "kernel": "fps_rounds_cluster" if loop_mode in (2, 3) else "fps_loop_cluster",
                          "algorithmic_bytes_per_launch": alg_bytes / args.steps,
                          "kernel_ms_per_launch": loop_ms / args.steps,
                          "points_evaluated_per_launch": evals / args.steps},
