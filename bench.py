@@ -26,6 +26,9 @@ runs the 256-scan batch split over the ranks instead (strong scaling).
 
 `--impl reference` times the reference CPU implementation alone on the same
 workload with the host threads it can use (rank 0 only under torchrun).
+
+`--path group [--radius R --nsample S]` measures the step after sampling
+instead: the ball query around the c2 scan's 16,384 FPS samples (run_group).
 """
 from __future__ import annotations
 
@@ -56,6 +59,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["fps", "group"], default="fps",
+                    help="fps: the sampler (default); group: the ball query after it")
+    ap.add_argument("--radius", type=float, default=0.5, help="--path group: ball radius")
+    ap.add_argument("--nsample", type=int, default=32, help="--path group: samples per ball")
     return ap.parse_args()
 
 
@@ -98,6 +105,11 @@ class ClockSampler:
             threading.Thread(target=self._read, daemon=True).start()
         except OSError:
             self.proc = None
+        # wait (bounded) for the first sample, so that a timed region shorter
+        # than the sampling period is still bracketed by samples
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < 3.0:
+            time.sleep(0.01)
         return self
 
     def _read(self):
@@ -106,6 +118,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            n, t0 = len(self.lines), time.time()
+            while len(self.lines) <= n and time.time() - t0 < 1.0:  # one sample after
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -342,8 +357,124 @@ def run_ours(args):
     return 0
 
 
+def run_group(args):
+    """--path group: the ball query after sampling (one GPU, rank 0 of N
+    replicas).  Workload: the c2 scan, its 16,384 FPS samples as centres
+    (computed once, untimed), radius --radius, --nsample per ball.  A step is
+    one nsfps_ball_query_device call (grid build + query); `e2e` is
+    nsfps_ball_query with host buffers (points and centres in, indices and
+    hit counts out).  The reference has no ball query, so there is no
+    reference arm; cpu_baseline is the brute-force restatement (oracle, one
+    thread) on the first 1,024 centres."""
+    import torch
+    rank, local, world = D.env_rank()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    D.init("nccl", timeout_s=300)
+    from ns_fps_b200 import capi
+    cfg = S.CONFIGS["c2"]
+    cloud = S.lidar_scan(seed=rank)
+    d_xyz = torch.from_numpy(cloud).to(dev)
+    d_s = torch.empty(cfg.k, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    n_s = capi.fps_device(d_xyz.data_ptr(), [0, cfg.n], cfg.k, (cfg.rng, cfg.blocks), False,
+                          d_s.data_ptr(), stream.cuda_stream)[0]
+    centers = d_xyz[d_s[:n_s]].contiguous()
+    m, S_, radius = int(n_s), int(args.nsample), float(args.radius)
+    d_idx = torch.empty((m, S_), dtype=torch.int64, device=dev)
+    d_hits = torch.empty(m, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        capi.ball_query_device(d_xyz.data_ptr(), [0, cfg.n], centers.data_ptr(), [0, m], radius,
+                               S_, d_idx.data_ptr(), d_hits.data_ptr(), stream.cuda_stream)
+
+    capi.set_profiling(True)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    D.barrier(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    q_ms, g_ms, launches = 0.0, 0.0, 0
+    with ClockSampler(local) as clk:
+        for s in range(args.steps):
+            flush.zero_()
+            ev[s][0].record(stream)
+            step()
+            ev[s][1].record(stream)
+            prof = capi.last_profile()
+            q_ms += prof.loop_ms
+            g_ms += prof.setup_ms
+            launches += prof.launches
+        torch.cuda.synchronize(dev)
+    my_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    D.barrier(local)
+    host_pts, host_c = cloud, centers.cpu().numpy()
+    e2e = []
+    for s in range(max(1, args.steps // 2) + 1):
+        t0 = time.perf_counter()
+        capi.ball_query(host_pts, host_c, radius, S_, device=local)
+        if s:
+            e2e.append(time.perf_counter() - t0)
+    e2e_s = float(np.mean(e2e))
+    total_ms, e2e_max = D.max_over_ranks([my_ms, e2e_s], device=dev)
+    result = None
+    if rank == 0:
+        # algorithmic bytes of the query kernel: points (12 B) and centres
+        # (12 B) read once, the index rows (8 B per slot) and hit counts written
+        alg = 12.0 * cfg.n + 12.0 * m + 8.0 * m * S_ + 4.0 * m
+        q_launch_ms = q_ms / args.steps
+        achieved = alg / (q_launch_ms / 1e3) / 1e9
+        peak, peak_kind = measured_peaks()
+        result = {
+            "metric": "ball queries/s after FPS (c2 scan, 16,384 centres)", "path": "group",
+            "value": world * m / (total_ms / 1e3 / args.steps), "unit": "queries/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "c2 + ball query", "points": cfg.n, "centres": m,
+                       "radius": radius, "nsample": S_,
+                       "l2": "256 MiB flush between steps, outside the timed window"},
+            "grid_build_ms": g_ms / args.steps, "query_kernel_ms": q_launch_ms,
+            "mean_hits": float(d_hits.float().mean().item()),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "kernel": "ball_query", "algorithmic_bytes_per_launch": alg,
+                         "kernel_ms_per_launch": q_launch_ms},
+            "e2e": {"value": world * m / e2e_max, "unit": "queries/s",
+                    "h2d_bytes_per_step": int(12 * cfg.n + 12 * m),
+                    "d2h_bytes_per_step": int(8 * m * S_ + 4 * m)},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            t0 = time.perf_counter()
+            oracle.ball_query(host_pts, host_c[:1024], radius, S_)
+            dt = time.perf_counter() - t0
+            result["cpu_baseline"] = {"value": 1024 / dt, "unit": "queries/s", "cores": 1,
+                                      "kind": "port",
+                                      "sample": f"brute-force restatement, first 1024 centres, "
+                                                f"{dt:.2f} s"}
+    D.barrier(local)
+    D.finalize()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.path == "group":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "path": "group",
+                              "unavailable": "the reference has no ball query"}), flush=True)
+            return 0
+        return run_group(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -191,6 +191,60 @@ NSFPS_API int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k
                             const nsfps_range *range, uint64_t *d_out,
                             uint64_t *out_len, void *stream);
 
+/* ---- Grouping after sampling.  No counterpart in the reference, which stops
+ * at the sample indices (src/yuezu_fps.cpp:676-730, yuezu_fps_pybind.cpp:
+ * 137-143); these are the operators a PointNet++-style pipeline applies to
+ * them next.
+ *
+ * Ball query (PointNet++ query_ball_point semantics): for centre j, the first
+ * `nsample` points k of its cloud in index order with d2 < radius * radius,
+ * d2 = (dx*dx + dy*dy) + dz*dz, dx = x_k - cx, every operation fp32 rounded
+ * to nearest with no multiply-add contraction (the sampler's distance,
+ * src/yuezu_fps.cpp:205-209).  idx[j * nsample + s] holds point indices
+ * within the cloud, ascending; slots past the hits repeat the first hit; a
+ * centre with no hit gets 0 in every slot.  hits[j] = min(number of hits,
+ * nsample).  Points with a non-finite coordinate are never hits; a negative
+ * radius acts as its magnitude, a NaN or zero radius finds nothing. */
+#define NSFPS_MAX_NSAMPLE 1024u
+
+/* Device-resident, batched: `count` clouds packed in d_xyz
+ * (point_offsets[i]..point_offsets[i+1]) and their centres packed in
+ * d_centers (center_offsets[i]..center_offsets[i+1]); offsets in HOST memory
+ * (count + 1 entries each).  d_idx (m x nsample int64) and d_hits (m uint32,
+ * may be NULL) are DEVICE buffers indexed from the first centre of the call.
+ * Work is issued on `stream` of the current device; the call returns after
+ * the stream has drained (the per-device workspace is reused by the next
+ * call).  Inputs are not modified. */
+NSFPS_API int nsfps_ball_query_device(const float *d_xyz, const uint64_t *point_offsets,
+                            const float *d_centers, const uint64_t *center_offsets,
+                            uint64_t count, float radius, uint32_t nsample, int64_t *d_idx,
+                            uint32_t *d_hits, void *stream);
+
+/* The same for one cloud in HOST memory (n x 3 points, m x 3 centres);
+ * idx (m x nsample) and hits (m, may be NULL) are HOST buffers. */
+NSFPS_API int nsfps_ball_query(const float *xyz, uint64_t n, const float *centers, uint64_t m,
+                     float radius, uint32_t nsample, int64_t *idx, uint32_t *hits,
+                     int device);
+
+/* Gather of sampled points (PointNet++ gather_operation on coordinates):
+ * d_out[3j + a] = coordinate a of point d_idx[j] of entry j's cloud; entries
+ * packed per cloud by idx_offsets (HOST, count + 1), points by point_offsets.
+ * Device buffers, current device, returns after `stream` drained.  An index
+ * outside its cloud gives NaNs at its entry and NSFPS_ERR_ARG. */
+NSFPS_API int nsfps_gather_points_device(const float *d_xyz, const uint64_t *point_offsets,
+                               const int64_t *d_idx, const uint64_t *idx_offsets,
+                               uint64_t count, float *d_out, void *stream);
+
+/* Grouped coordinates relative to each centre (PointNet++ grouping of
+ * xyz followed by the subtraction of the centre): d_out[((j * nsample) + s)
+ * * 3 + a] = xyz[d_idx[j * nsample + s]][a] - centers[j][a] (fp32, round to
+ * nearest), d_idx as written by nsfps_ball_query_device.  Errors as in
+ * nsfps_gather_points_device. */
+NSFPS_API int nsfps_group_points_device(const float *d_xyz, const uint64_t *point_offsets,
+                              const float *d_centers, const uint64_t *center_offsets,
+                              uint64_t count, uint32_t nsample, const int64_t *d_idx,
+                              float *d_out, void *stream);
+
 /* Timing and work counters of the last call on this thread: stage times in
  * milliseconds measured with CUDA events on the launching stream (setup =
  * binning, sort and leaf build; loop = the persistent sampling kernel;
@@ -200,7 +254,9 @@ NSFPS_API int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k
  * bounding-box skip, and the loop configuration (CTAs per cloud and mode:
  * 0 = per-step cluster loop, 2 = round-based cluster loop, 3 = round-based
  * loop over co-resident CTAs for one cloud larger than a cluster's shared
- * memory).  Enabled by nsfps_set_profiling. */
+ * memory).  After a ball query (mode 4): setup = the grid build, loop = the
+ * query kernel, launches = its kernel launches; the work counters are 0.
+ * Enabled by nsfps_set_profiling. */
 typedef struct nsfps_profile {
   float setup_ms, loop_ms, total_ms;
   uint32_t launches;

@@ -24,7 +24,7 @@ EXT = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
 MODULE = os.path.join(HERE, "yuezu_fps_module" + EXT)
 
 CU_SOURCES = ["nsfps_setup.cu", "nsfps_loop.cu", "nsfps_rounds.cu", "nsfps_static.cu",
-              "nsfps_capi.cu"]
+              "nsfps_group.cu", "nsfps_capi.cu"]
 HEADERS = ["nsfps_internal.cuh", "nsfps_kernels.h", "nsfps_device.cuh"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -155,3 +155,65 @@ def fps_device_static(d_xyz_ptr: int, n: int, k: int, bounds, blocks, d_out_ptr:
     if rc != OK:
         raise RuntimeError(f"nsfps_fps_device_static rc={rc}: {last_error()}")
     return int(ln.value)
+
+
+# ---------------------------------------------------------------- grouping
+
+def _offsets(offsets):
+    return (ctypes.c_uint64 * len(offsets))(*[int(o) for o in offsets])
+
+
+def ball_query(points, centers, radius: float, nsample: int, device: int = 0):
+    """nsfps_ball_query: one cloud and its centres in host memory.  Returns
+    (idx int64 (M, nsample), hits uint32 (M,))."""
+    p = np.ascontiguousarray(np.asarray(points, dtype=np.float32))
+    c = np.ascontiguousarray(np.asarray(centers, dtype=np.float32))
+    m = c.shape[0]
+    idx = np.zeros((m, max(int(nsample), 1)), dtype=np.int64)
+    hits = np.zeros(m, dtype=np.uint32)
+    rc = lib().nsfps_ball_query(p.ctypes.data_as(_f32p), ctypes.c_uint64(p.shape[0]),
+                                c.ctypes.data_as(_f32p), ctypes.c_uint64(m),
+                                ctypes.c_float(radius), ctypes.c_uint32(int(nsample)),
+                                idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                hits.ctypes.data_as(_u32p), ctypes.c_int(device))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_ball_query rc={rc}: {last_error()}")
+    return idx, hits
+
+
+def ball_query_device(d_xyz_ptr: int, point_offsets, d_centers_ptr: int, center_offsets,
+                      radius: float, nsample: int, d_idx_ptr: int, d_hits_ptr: int = 0,
+                      stream_ptr: int = 0):
+    """nsfps_ball_query_device on packed device-resident clouds and centres."""
+    count = len(point_offsets) - 1
+    rc = lib().nsfps_ball_query_device(
+        ctypes.c_void_p(d_xyz_ptr), _offsets(point_offsets), ctypes.c_void_p(d_centers_ptr),
+        _offsets(center_offsets), ctypes.c_uint64(count), ctypes.c_float(radius),
+        ctypes.c_uint32(int(nsample)), ctypes.c_void_p(d_idx_ptr),
+        ctypes.c_void_p(d_hits_ptr or None), ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_ball_query_device rc={rc}: {last_error()}")
+
+
+def gather_points_device(d_xyz_ptr: int, point_offsets, d_idx_ptr: int, idx_offsets,
+                         d_out_ptr: int, stream_ptr: int = 0):
+    """nsfps_gather_points_device."""
+    count = len(point_offsets) - 1
+    rc = lib().nsfps_gather_points_device(
+        ctypes.c_void_p(d_xyz_ptr), _offsets(point_offsets), ctypes.c_void_p(d_idx_ptr),
+        _offsets(idx_offsets), ctypes.c_uint64(count), ctypes.c_void_p(d_out_ptr),
+        ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_gather_points_device rc={rc}: {last_error()}")
+
+
+def group_points_device(d_xyz_ptr: int, point_offsets, d_centers_ptr: int, center_offsets,
+                        nsample: int, d_idx_ptr: int, d_out_ptr: int, stream_ptr: int = 0):
+    """nsfps_group_points_device."""
+    count = len(point_offsets) - 1
+    rc = lib().nsfps_group_points_device(
+        ctypes.c_void_p(d_xyz_ptr), _offsets(point_offsets), ctypes.c_void_p(d_centers_ptr),
+        _offsets(center_offsets), ctypes.c_uint64(count), ctypes.c_uint32(int(nsample)),
+        ctypes.c_void_p(d_idx_ptr), ctypes.c_void_p(d_out_ptr), ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_group_points_device rc={rc}: {last_error()}")

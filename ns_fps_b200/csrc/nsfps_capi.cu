@@ -696,6 +696,153 @@ void fill_trivial(uint64_t n, uint64_t k, uint64_t *out, uint64_t *len) {
   *len = n;
 }
 
+// ---- grouping after sampling
+
+// offsets[0..count] (host, non-decreasing) relative to offsets[0], as uint32.
+int rel_offsets(const uint64_t *offsets, uint64_t count, const char *what,
+                std::vector<uint32_t> &out) {
+  out.resize(count + 1);
+  for (uint64_t i = 0; i <= count; ++i) {
+    if (i < count && offsets[i + 1] < offsets[i])
+      return set_error(NSFPS_ERR_ARG, "%s must not decrease", what);
+    if (offsets[i] - offsets[0] >= (1ull << 31))
+      return set_error(NSFPS_ERR_UNSUPPORTED, "too many entries in %s (>= 2^31)", what);
+    out[i] = (uint32_t)(offsets[i] - offsets[0]);
+  }
+  return NSFPS_OK;
+}
+
+struct GroupBuffers {
+  uint32_t *poff, *coff, *cbase, *keys0, *vals0, *keys1, *vals1, *hist, *partial, *cstart;
+  uint32_t *box;
+  GroupGrid *grids;
+  float4 *pts;
+};
+
+size_t carve_group(Carver &c, uint32_t B, uint32_t n, uint32_t cells, GroupBuffers &b) {
+  const size_t tiles = (n + 4095) / 4096;
+  const size_t scan_len = std::max<size_t>(256 * tiles, (size_t)cells + 1);
+  b.poff = c.take<uint32_t>(B + 1);
+  b.coff = c.take<uint32_t>(B + 1);
+  b.cbase = c.take<uint32_t>(B + 1);
+  b.box = c.take<uint32_t>(6 * (size_t)B);
+  b.grids = c.take<GroupGrid>(B);
+  b.keys0 = c.take<uint32_t>(n);
+  b.vals0 = c.take<uint32_t>(n);
+  b.keys1 = c.take<uint32_t>(n);
+  b.vals1 = c.take<uint32_t>(n);
+  b.hist = c.take<uint32_t>(256 * tiles + 1);
+  b.partial = c.take<uint32_t>((scan_len + 4095) / 4096 + 2);
+  b.cstart = c.take<uint32_t>((size_t)cells + 1);
+  b.pts = c.take<float4>(n);
+  return align_up(c.off, 256);
+}
+
+// Cells a cloud of nc points may use: about two per point, at least 4096, at
+// most 2^22.
+uint32_t group_cell_cap(uint32_t nc) {
+  const uint64_t want = std::max<uint64_t>(4096u, 2ull * nc);
+  return (uint32_t)std::min<uint64_t>(want, 1u << 22);
+}
+
+// Ball query of packed device-resident clouds (poff / coff: host offsets)
+// on stream st; returns after the stream has drained.
+int ball_query_on(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz,
+                  const std::vector<uint32_t> &poff, const float *d_centers,
+                  const std::vector<uint32_t> &coff, float radius, uint32_t S, int64_t *d_idx,
+                  uint32_t *d_hits) {
+  const uint32_t B = (uint32_t)(poff.size() - 1);
+  const uint32_t n = poff[B], m = coff[B];
+  if (m == 0) return NSFPS_OK;
+  const float rr = std::fabs(radius);
+  if (!(rr > 0.0f)) {
+    // radius 0 or NaN: d2 < r2 holds for no point; every slot is index 0
+    NSFPS_CUDA(cudaMemsetAsync(d_idx, 0, sizeof(int64_t) * (size_t)m * S, st));
+    if (d_hits) NSFPS_CUDA(cudaMemsetAsync(d_hits, 0, sizeof(uint32_t) * (size_t)m, st));
+    NSFPS_CUDA(cudaStreamSynchronize(st));
+    return NSFPS_OK;
+  }
+  std::vector<uint32_t> cbase(B + 1);
+  uint64_t cells = 0;
+  for (uint32_t c = 0; c < B; ++c) {
+    cbase[c] = (uint32_t)cells;
+    cells += group_cell_cap(poff[c + 1] - poff[c]);
+    if (cells >= (1ull << 31))
+      return set_error(NSFPS_ERR_UNSUPPORTED, "too many clouds in one ball query");
+  }
+  cbase[B] = (uint32_t)cells;
+  GroupBuffers b{};
+  Carver dry(nullptr);
+  const size_t need = carve_group(dry, B, n, (uint32_t)cells, b);
+  int rc = ensure_ws(ctx, need);
+  if (rc) return rc;
+  Carver cv(ctx->ws);
+  carve_group(cv, B, n, (uint32_t)cells, b);
+  NSFPS_CUDA(cudaMemcpyAsync(b.poff, poff.data(), 4 * (B + 1), cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.coff, coff.data(), 4 * (B + 1), cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(b.cbase, cbase.data(), 4 * (B + 1), cudaMemcpyHostToDevice, st));
+  GroupArgs a{};
+  a.n = n; a.B = B; a.m = m; a.S = S;
+  a.max_cloud = 0;
+  for (uint32_t c = 0; c < B; ++c) a.max_cloud = std::max(a.max_cloud, poff[c + 1] - poff[c]);
+  a.cells = (uint32_t)cells;
+  a.r2 = radius * radius;
+  a.h_min = 1.01 * (double)rr;
+  a.xyz = d_xyz; a.centers = d_centers;
+  a.poff = b.poff; a.coff = b.coff; a.cbase = b.cbase;
+  a.box = b.box; a.grids = b.grids;
+  a.keys0 = b.keys0; a.vals0 = b.vals0; a.keys1 = b.keys1; a.vals1 = b.vals1;
+  a.hist = b.hist; a.partial = b.partial; a.cstart = b.cstart; a.pts = b.pts;
+  a.out_idx = d_idx; a.out_hits = d_hits;
+  uint32_t launches = 0;
+  const bool prof = g_profiling.load() != 0;
+  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[0], st));
+  NSFPS_CUDA(run_ball_query(a, st, launches, prof ? ctx->ev[1] : nullptr,
+                            prof ? ctx->ev[2] : nullptr));
+  NSFPS_CUDA(cudaStreamSynchronize(st));
+  if (prof) {
+    // setup = grid build (box, cells, sort, cell starts); loop = query kernel
+    g_prof = nsfps_profile{};
+    cudaEventElapsedTime(&g_prof.setup_ms, ctx->ev[0], ctx->ev[1]);
+    cudaEventElapsedTime(&g_prof.loop_ms, ctx->ev[1], ctx->ev[2]);
+    cudaEventElapsedTime(&g_prof.total_ms, ctx->ev[0], ctx->ev[2]);
+    g_prof.launches = launches;
+    g_prof.mode = 4;
+  }
+  return NSFPS_OK;
+}
+
+// Gather (ctr == nullptr) or relative grouping of device-resident clouds:
+// the index check's flag comes back through the workspace.
+int gather_on(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz,
+              const std::vector<uint32_t> &poff, const float *d_centers,
+              const std::vector<uint32_t> &ioff, uint32_t S, const int64_t *d_idx, float *d_out) {
+  const uint32_t B = (uint32_t)(poff.size() - 1);
+  const uint32_t m = ioff[B];
+  if (m == 0) return NSFPS_OK;
+  const size_t off_bytes = align_up(sizeof(uint32_t) * (B + 1), 256);
+  int rc = ensure_ws(ctx, 2 * off_bytes + 256);
+  if (rc) return rc;
+  uint32_t *d_poff = (uint32_t *)ctx->ws;
+  uint32_t *d_ioff = (uint32_t *)((char *)ctx->ws + off_bytes);
+  uint32_t *d_err = (uint32_t *)((char *)ctx->ws + 2 * off_bytes);
+  NSFPS_CUDA(cudaMemcpyAsync(d_poff, poff.data(), 4 * (B + 1), cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemcpyAsync(d_ioff, ioff.data(), 4 * (B + 1), cudaMemcpyHostToDevice, st));
+  NSFPS_CUDA(cudaMemsetAsync(d_err, 0, sizeof(uint32_t), st));
+  uint32_t launches = 0;
+  if (d_centers)
+    NSFPS_CUDA(run_group_points(d_xyz, d_poff, d_centers, d_ioff, B, m, S, d_idx, d_out, d_err, st,
+                                launches));
+  else
+    NSFPS_CUDA(run_gather_points(d_xyz, d_poff, d_idx, d_ioff, B, m, d_out, d_err, st, launches));
+  uint32_t herr = 0;
+  NSFPS_CUDA(cudaMemcpyAsync(&herr, d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaStreamSynchronize(st));
+  if (herr)
+    return set_error(NSFPS_ERR_ARG, "an index lies outside its cloud (its output is NaN)");
+  return NSFPS_OK;
+}
+
 // Batched host-memory path on one device.
 int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
                       const std::vector<uint64_t> &idx, uint64_t k,
@@ -1031,6 +1178,131 @@ int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k,
   if (rc) return rc;
   *out_len = lens[0];
   return NSFPS_OK;
+}
+
+int nsfps_ball_query_device(const float *d_xyz, const uint64_t *point_offsets,
+                            const float *d_centers, const uint64_t *center_offsets,
+                            uint64_t count, float radius, uint32_t nsample, int64_t *d_idx,
+                            uint32_t *d_hits, void *stream) {
+  clear_error();
+  if (count == 0) return NSFPS_OK;
+  if (!point_offsets || !center_offsets) return set_error(NSFPS_ERR_ARG, "NULL offsets");
+  if (nsample == 0 || nsample > NSFPS_MAX_NSAMPLE)
+    return set_error(NSFPS_ERR_ARG, "nsample must be in 1..%u", NSFPS_MAX_NSAMPLE);
+  std::vector<uint32_t> poff, coff;
+  int rc = rel_offsets(point_offsets, count, "point_offsets", poff);
+  if (rc) return rc;
+  rc = rel_offsets(center_offsets, count, "center_offsets", coff);
+  if (rc) return rc;
+  if ((poff[count] && !d_xyz) || (coff[count] && (!d_centers || !d_idx)))
+    return set_error(NSFPS_ERR_ARG, "NULL argument");
+  int dev = 0;
+  NSFPS_CUDA(cudaGetDevice(&dev));
+  DeviceCtx *ctx = nullptr;
+  rc = get_ctx(dev, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (d_xyz) d_xyz += 3 * point_offsets[0];
+  if (d_centers) d_centers += 3 * center_offsets[0];
+  return ball_query_on(ctx, (cudaStream_t)stream, d_xyz, poff, d_centers, coff, radius, nsample,
+                       d_idx, d_hits);
+}
+
+int nsfps_ball_query(const float *xyz, uint64_t n, const float *centers, uint64_t m,
+                     float radius, uint32_t nsample, int64_t *idx, uint32_t *hits, int device) {
+  clear_error();
+  if (nsample == 0 || nsample > NSFPS_MAX_NSAMPLE)
+    return set_error(NSFPS_ERR_ARG, "nsample must be in 1..%u", NSFPS_MAX_NSAMPLE);
+  if (m == 0) return NSFPS_OK;
+  if ((n && !xyz) || !centers || !idx) return set_error(NSFPS_ERR_ARG, "NULL argument");
+  if (n >= (1ull << 31) || m >= (1ull << 31))
+    return set_error(NSFPS_ERR_UNSUPPORTED, "too many points or centres (>= 2^31)");
+  DeviceCtx *ctx = nullptr;
+  int rc = get_ctx(device, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  NSFPS_CUDA(cudaSetDevice(device));
+  cudaStream_t st = ctx->stream;
+  const size_t bx = sizeof(float) * 3 * std::max<uint64_t>(n, 1);
+  const size_t bc = sizeof(float) * 3 * m, bi = sizeof(int64_t) * m * nsample,
+               bh = sizeof(uint32_t) * m;
+  void *io = nullptr;
+  NSFPS_CUDA(cudaMallocAsync(&io, align_up(bx, 256) + align_up(bc, 256) + align_up(bi, 256) + bh, st));
+  char *p = (char *)io;
+  float *d_xyz = (float *)p;
+  float *d_c = (float *)(p + align_up(bx, 256));
+  int64_t *d_idx = (int64_t *)(p + align_up(bx, 256) + align_up(bc, 256));
+  uint32_t *d_hits = (uint32_t *)(p + align_up(bx, 256) + align_up(bc, 256) + align_up(bi, 256));
+  std::vector<uint32_t> poff = {0u, (uint32_t)n}, coff = {0u, (uint32_t)m};
+  rc = NSFPS_OK;
+  cudaError_t e = cudaSuccess;
+  if (n) e = cudaMemcpyAsync(d_xyz, xyz, sizeof(float) * 3 * n, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_c, centers, bc, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) {
+    rc = set_error(NSFPS_ERR_CUDA, "copy to the device failed: %s", cudaGetErrorString(e));
+  } else {
+    rc = ball_query_on(ctx, st, d_xyz, poff, d_c, coff, radius, nsample, d_idx, d_hits);
+  }
+  if (rc == NSFPS_OK) {
+    e = cudaMemcpyAsync(idx, d_idx, bi, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && hits) e = cudaMemcpyAsync(hits, d_hits, bh, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+      rc = set_error(NSFPS_ERR_CUDA, "copy to the host failed: %s", cudaGetErrorString(e));
+  }
+  cudaFreeAsync(io, st);
+  cudaStreamSynchronize(st);
+  return rc;
+}
+
+int nsfps_gather_points_device(const float *d_xyz, const uint64_t *point_offsets,
+                               const int64_t *d_idx, const uint64_t *idx_offsets, uint64_t count,
+                               float *d_out, void *stream) {
+  clear_error();
+  if (count == 0) return NSFPS_OK;
+  if (!point_offsets || !idx_offsets) return set_error(NSFPS_ERR_ARG, "NULL offsets");
+  std::vector<uint32_t> poff, ioff;
+  int rc = rel_offsets(point_offsets, count, "point_offsets", poff);
+  if (rc) return rc;
+  rc = rel_offsets(idx_offsets, count, "idx_offsets", ioff);
+  if (rc) return rc;
+  if (ioff[count] && (!d_xyz || !d_idx || !d_out)) return set_error(NSFPS_ERR_ARG, "NULL argument");
+  int dev = 0;
+  NSFPS_CUDA(cudaGetDevice(&dev));
+  DeviceCtx *ctx = nullptr;
+  rc = get_ctx(dev, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (d_xyz) d_xyz += 3 * point_offsets[0];
+  return gather_on(ctx, (cudaStream_t)stream, d_xyz, poff, nullptr, ioff, 1, d_idx, d_out);
+}
+
+int nsfps_group_points_device(const float *d_xyz, const uint64_t *point_offsets,
+                              const float *d_centers, const uint64_t *center_offsets,
+                              uint64_t count, uint32_t nsample, const int64_t *d_idx,
+                              float *d_out, void *stream) {
+  clear_error();
+  if (count == 0) return NSFPS_OK;
+  if (!point_offsets || !center_offsets) return set_error(NSFPS_ERR_ARG, "NULL offsets");
+  if (nsample == 0 || nsample > NSFPS_MAX_NSAMPLE)
+    return set_error(NSFPS_ERR_ARG, "nsample must be in 1..%u", NSFPS_MAX_NSAMPLE);
+  std::vector<uint32_t> poff, coff;
+  int rc = rel_offsets(point_offsets, count, "point_offsets", poff);
+  if (rc) return rc;
+  rc = rel_offsets(center_offsets, count, "center_offsets", coff);
+  if (rc) return rc;
+  if (coff[count] && (!d_xyz || !d_centers || !d_idx || !d_out))
+    return set_error(NSFPS_ERR_ARG, "NULL argument");
+  int dev = 0;
+  NSFPS_CUDA(cudaGetDevice(&dev));
+  DeviceCtx *ctx = nullptr;
+  rc = get_ctx(dev, &ctx);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (d_xyz) d_xyz += 3 * point_offsets[0];
+  if (d_centers) d_centers += 3 * center_offsets[0];
+  return gather_on(ctx, (cudaStream_t)stream, d_xyz, poff, d_centers, coff, nsample, d_idx,
+                   d_out);
 }
 
 int nsfps_set_profiling(int enable) {

@@ -63,6 +63,18 @@ struct SetupArgs {
 
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches);
 
+// Stable LSD radix sort of n (key, value) pairs, 8-bit digits over the bits of
+// max_key.  *keys / *vals hold the input and, on return, point at whichever of
+// the two buffer pairs holds the sorted result.  hist: 256 * ceil(n / 4096)
+// + 1 entries; partial: ceil(256 * ceil(n / 4096) / 4096) + 2.
+cudaError_t run_sort_pairs(uint32_t **keys, uint32_t **vals, uint32_t *keys_alt,
+                           uint32_t *vals_alt, uint32_t n, uint32_t max_key, uint32_t *hist,
+                           uint32_t *partial, cudaStream_t st, uint32_t &launches);
+// Exclusive prefix sum of n uint32 (in may equal out); partial: ceil(n / 4096)
+// + 2 entries.
+cudaError_t run_exclusive_scan(const uint32_t *in, uint32_t *out, uint32_t n,
+                               uint32_t *partial, cudaStream_t st, uint32_t &launches);
+
 // compute_bbox of each of B device-resident clouds (poff: B + 1 point
 // offsets, device): out[6c .. 6c+5] = min x, y, z, max x, y, z.
 cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, float *out,
@@ -131,6 +143,50 @@ cudaError_t run_epilogue(const uint32_t *out_rank, const uint32_t *out_count,
 
 size_t loop_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t extra, uint32_t tab);
 int loop_max_smem();  // bytes of dynamic shared memory a CTA may use
+
+// ---- grouping after sampling (nsfps_group.cu)
+
+// Uniform grid of one cloud for the ball query: cell of a point on axis a =
+// floor((v - lo[a]) * inv[a]) (double), clamped to g[a] - 1; global cell id =
+// base + (cz * g[1] + cy) * g[0] + cx.
+struct GroupGrid {
+  double lo[3];
+  double inv[3];
+  uint32_t g[3];
+  uint32_t base;
+};
+
+struct GroupArgs {
+  uint32_t n, B, m, S;        // points, clouds, centres, samples per centre
+  uint32_t max_cloud;         // points of the largest cloud
+  uint32_t cells;             // cells over all clouds; key `cells` = no cell
+  float r2;                   // radius * radius (fp32)
+  double h_min;               // smallest cell width: 1.01 * |radius|
+  const float *xyz;           // n x 3 (device)
+  const float *centers;       // m x 3 (device)
+  const uint32_t *poff, *coff, *cbase;  // B + 1 point / centre / cell offsets
+  uint32_t *box;              // 6 * B: per-cloud box as ordered integers
+  GroupGrid *grids;           // B
+  uint32_t *keys0, *vals0, *keys1, *vals1;  // n each
+  uint32_t *hist, *partial;   // radix-sort histogram, scan partials
+  uint32_t *cstart;           // cells + 1: per-cell counts, then cell starts
+  float4 *pts;                // n sorted (x, y, z, point id bits)
+  int64_t *out_idx;           // m * S
+  uint32_t *out_hits;         // m, or null
+};
+
+int ball_query_warps(uint32_t S);
+size_t ball_query_smem(uint32_t S);
+// Grid build and query; the two events (may be null) bracket the query kernel.
+cudaError_t run_ball_query(const GroupArgs &a, cudaStream_t st, uint32_t &launches,
+                           cudaEvent_t ev_query_begin, cudaEvent_t ev_query_end);
+cudaError_t run_gather_points(const float *xyz, const uint32_t *poff, const int64_t *idx,
+                              const uint32_t *ioff, uint32_t B, uint32_t m, float *out,
+                              uint32_t *err_flag, cudaStream_t st, uint32_t &launches);
+cudaError_t run_group_points(const float *xyz, const uint32_t *poff, const float *centers,
+                             const uint32_t *coff, uint32_t B, uint32_t m, uint32_t S,
+                             const int64_t *idx, float *out, uint32_t *err_flag, cudaStream_t st,
+                             uint32_t &launches);
 
 // Address and size of the fixed scratch array (nsfps_static.cu) on the
 // current device.

@@ -467,6 +467,37 @@ cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, f
   return cudaGetLastError();
 }
 
+cudaError_t run_sort_pairs(uint32_t **keys, uint32_t **vals, uint32_t *keys_alt,
+                           uint32_t *vals_alt, uint32_t n, uint32_t max_key, uint32_t *hist,
+                           uint32_t *partial, cudaStream_t st, uint32_t &launches) {
+  if (n == 0) return cudaSuccess;
+  int bits = 0;
+  while (bits < 32 && ((max_key >> bits) != 0)) ++bits;
+  const int passes = (bits + 7) / 8;
+  uint32_t *kin = *keys, *vin = *vals, *kout = keys_alt, *vout = vals_alt;
+  const uint32_t ntiles = cdiv(n, kRsTile);
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = pass * 8;
+    radix_upsweep<<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, hist, ntiles);
+    device_scan<false, false>(hist, hist, 256u * ntiles, partial, st, launches);
+    radix_downsweep<<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift, hist,
+                                                   ntiles);
+    launches += 2;
+    uint32_t *t;
+    t = kin; kin = kout; kout = t;
+    t = vin; vin = vout; vout = t;
+  }
+  *keys = kin;
+  *vals = vin;
+  return cudaGetLastError();
+}
+
+cudaError_t run_exclusive_scan(const uint32_t *in, uint32_t *out, uint32_t n,
+                               uint32_t *partial, cudaStream_t st, uint32_t &launches) {
+  device_scan<false, false>(in, out, n, partial, st, launches);
+  return cudaGetLastError();
+}
+
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
   const uint32_t n = a.n;
   const uint32_t B = a.B;
@@ -478,23 +509,10 @@ cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
   launches += 1;
 
   // radix passes cover the largest possible key (total buckets - 1)
-  int bits = 0;
-  while (bits < 32 && ((a.max_key >> bits) != 0)) ++bits;
-  const int passes = (bits + 7) / 8;
-
-  uint32_t *kin = a.keys0, *vin = a.vals0, *kout = a.keys1, *vout = a.vals1;
-  const uint32_t ntiles = cdiv(n, kRsTile);
-  for (int pass = 0; pass < passes; ++pass) {
-    const int shift = pass * 8;
-    radix_upsweep<<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, a.hist, ntiles);
-    device_scan<false, false>(a.hist, a.hist, 256u * ntiles, a.partial, st, launches);
-    radix_downsweep<<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift,
-                                                   a.hist, ntiles);
-    launches += 2;
-    uint32_t *t;
-    t = kin; kin = kout; kout = t;
-    t = vin; vin = vout; vout = t;
-  }
+  uint32_t *kin = a.keys0, *vin = a.vals0;
+  if ((err = run_sort_pairs(&kin, &vin, a.keys1, a.vals1, n, a.max_key, a.hist, a.partial,
+                            st, launches)))
+    return err;
   // kin / vin now hold the sorted keys and point ids
   gather_points<<<cdiv(n, 256), 256, 0, st>>>(kin, vin, a.xyz, n, a.poff, B, a.pts,
                                               a.perm, a.tmp0);

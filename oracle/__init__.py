@@ -132,6 +132,43 @@ def bin_points(points, rng, blocks):
     return cells, buckets
 
 
+def ball_query(points, centers, radius: float, nsample: int):
+    """Restated PointNet++ ball query (brute force, ``nsfps_oracle_ball_query``):
+    (idx int64 (M, nsample), hits uint32 (M,)).  Not part of the reference."""
+    lib = _load(ORACLE_SO)
+    p = _pts(points)
+    c = _pts(centers)
+    m = c.shape[0]
+    idx = np.zeros((m, max(int(nsample), 1)), dtype=np.int64)
+    hits = np.zeros(m, dtype=np.uint32)
+    lib.nsfps_oracle_ball_query(p.ctypes.data_as(_f32p), ctypes.c_uint64(p.shape[0]),
+                                c.ctypes.data_as(_f32p), ctypes.c_uint64(m),
+                                ctypes.c_float(radius), ctypes.c_uint32(int(nsample)),
+                                idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                hits.ctypes.data_as(_u32p))
+    return idx, hits
+
+
+def ball_query_numpy(points, centers, radius: float, nsample: int):
+    """The same definition vectorised in numpy float32 (each operation rounded
+    separately, no FMA): an independent restatement for checking the C one."""
+    p = _pts(points)
+    c = _pts(centers)
+    idx = np.zeros((c.shape[0], int(nsample)), dtype=np.int64)
+    hits = np.zeros(c.shape[0], dtype=np.uint32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        r2 = np.float32(radius) * np.float32(radius)
+        for j in range(c.shape[0]):
+            d = p - c[j]
+            d2 = (d[:, 0] * d[:, 0] + d[:, 1] * d[:, 1]) + d[:, 2] * d[:, 2]
+            h = np.nonzero(d2 < r2)[0][: int(nsample)]
+            hits[j] = len(h)
+            if len(h):
+                idx[j, :] = h[0]
+                idx[j, : len(h)] = h
+    return idx, hits
+
+
 # ---------------------------------------------------------------- reference
 
 def ref_fps(points, k: int, rng: Optional[Sequence[float]], blocks: Sequence[int],

@@ -481,3 +481,38 @@ int nsfps_oracle_bin(const float *xyz, uint64_t n, const float rng[6],
   or_range_free(&r);
   return OR_OK;
 }
+
+/* ---- Grouping after sampling.  The reference stops at the sample indices
+ * (src/yuezu_fps.cpp:676-730) and has no ball query, so this part is not
+ * pinned against it: it restates the PointNet++ query_ball_point definition
+ * by brute force, with the sampler's distance (or_sqd, no FMA).  For each
+ * centre, walk the points in index order, keep those with
+ * d2 < radius * radius, stop after nsample; the remaining slots repeat the
+ * first hit, or hold 0 when there is none.  hits[j] = number kept. */
+int nsfps_oracle_ball_query(const float *xyz, uint64_t n, const float *centers,
+                            uint64_t m, float radius, uint32_t nsample,
+                            int64_t *idx, uint32_t *hits) {
+  const float r2 = radius * radius;
+  for (uint64_t j = 0; j < m; ++j) {
+    const float cx = centers[3 * j], cy = centers[3 * j + 1],
+                cz = centers[3 * j + 2];
+    int64_t *row = idx + j * (uint64_t)nsample;
+    uint32_t cnt = 0;
+    for (uint64_t k = 0; k < n && cnt < nsample; ++k) {
+      const float d2 =
+          or_sqd(xyz[3 * k], xyz[3 * k + 1], xyz[3 * k + 2], cx, cy, cz);
+      if (d2 < r2) {
+        if (cnt == 0)
+          for (uint32_t l = 0; l < nsample; ++l)
+            row[l] = (int64_t)k;
+        row[cnt++] = (int64_t)k;
+      }
+    }
+    if (cnt == 0)
+      for (uint32_t l = 0; l < nsample; ++l)
+        row[l] = 0;
+    if (hits)
+      hits[j] = cnt;
+  }
+  return OR_OK;
+}
