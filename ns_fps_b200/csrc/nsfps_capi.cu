@@ -294,7 +294,7 @@ constexpr uint32_t kGridMinPoints = NSFPS_GRID_MIN_POINTS;
 
 size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   const size_t n = j.n;
-  const size_t tiles = (n + 4095) / 4096;
+  const size_t tiles = radix_tiles(j.n);
   const size_t scan_len = std::max(n, 256 * tiles);
   b.xyz = own_xyz ? c.take<float>(3 * n) : nullptr;
   b.keys0 = c.take<uint32_t>(n);
@@ -720,7 +720,7 @@ struct GroupBuffers {
 };
 
 size_t carve_group(Carver &c, uint32_t B, uint32_t n, uint32_t cells, GroupBuffers &b) {
-  const size_t tiles = (n + 4095) / 4096;
+  const size_t tiles = radix_tiles(n);
   const size_t scan_len = std::max<size_t>(256 * tiles, (size_t)cells + 1);
   b.poff = c.take<uint32_t>(B + 1);
   b.coff = c.take<uint32_t>(B + 1);
@@ -738,10 +738,10 @@ size_t carve_group(Carver &c, uint32_t B, uint32_t n, uint32_t cells, GroupBuffe
   return align_up(c.off, 256);
 }
 
-// Cells a cloud of nc points may use: about two per point, at least 4096, at
-// most 2^22.
+// Cells a cloud of nc points may use: up to 16 per point (so that cells
+// stay about one radius wide in sparse clouds), at least 4096, at most 2^22.
 uint32_t group_cell_cap(uint32_t nc) {
-  const uint64_t want = std::max<uint64_t>(4096u, 2ull * nc);
+  const uint64_t want = std::max<uint64_t>(4096u, 16ull * nc);
   return (uint32_t)std::min<uint64_t>(want, 1u << 22);
 }
 

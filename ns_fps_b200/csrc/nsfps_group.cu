@@ -180,7 +180,32 @@ group_gather(const uint32_t *__restrict__ vals, const float *__restrict__ xyz, u
                        __uint_as_float(i));
 }
 
-// One warp per centre.  Shared memory: 27 * S point ids per warp.
+__device__ __forceinline__ uint32_t lanes_below(uint32_t x) {
+  return x >= 32u ? kFull : (1u << x) - 1u;
+}
+
+// Largest s in [0, 26] with shfl(key, s) <= v (key non-decreasing over lanes
+// 0..26; key[0] <= v).  All lanes take part.
+__device__ __forceinline__ uint32_t last_le(uint32_t key, uint32_t v) {
+  uint32_t s = 0;
+#pragma unroll
+  for (uint32_t step = 16; step; step >>= 1) {
+    const uint32_t cand = s + step;
+    const uint32_t kc = __shfl_sync(kFull, key, cand < 27u ? cand : 26u);
+    if (cand < 27u && kc <= v) s = cand;
+  }
+  return s;
+}
+
+// One warp per centre.  Shared memory: 27 * S point ids per warp, the kept
+// hits of neighbour cell s (ascending, as the cell's points are in index
+// order) at [s * S, s * S + kept_s).
+//
+// The 27 neighbour cells are scanned as one concatenated range of L points,
+// 32 per step: lane l takes position v0 + l, finds its cell by a binary search
+// over the cells' starts in that range, and a hit's rank in its cell is the
+// cell's earlier hits plus the hits of the lanes before it in the same cell
+// (a cell's positions are contiguous lanes of the step).
 __global__ void __launch_bounds__(256)
 ball_query(const float4 *__restrict__ pts, const uint32_t *__restrict__ cstart,
            const GroupGrid *__restrict__ grids, const uint32_t *__restrict__ poff,
@@ -200,79 +225,103 @@ ball_query(const float4 *__restrict__ pts, const uint32_t *__restrict__ cstart,
     const int cx = centre_cell(qx, gr.lo[0], gr.inv[0], gr.g[0]);
     const int cy = centre_cell(qy, gr.lo[1], gr.inv[1], gr.g[1]);
     const int cz = centre_cell(qz, gr.lo[2], gr.inv[2], gr.g[2]);
-    const int gx = (int)gr.g[0], gy = (int)gr.g[1], gz = (int)gr.g[2];
-    const int x0 = max(cx - 1, 0), x1 = min(cx + 1, gx - 1);
-    uint32_t cnt = 0;  // lane s < 27: hits kept for neighbour cell s
-    if (x0 <= x1) {
-      const uint32_t nc = (uint32_t)(x1 - x0 + 1);  // cells of a row (1..3)
-      for (int r = 0; r < 9; ++r) {
-        const int y = cy + (r % 3) - 1, z = cz + (r / 3) - 1;
-        if (y < 0 || y >= gy || z < 0 || z >= gz) continue;
-        const uint32_t row = gr.base + ((uint32_t)z * (uint32_t)gy + (uint32_t)y) * (uint32_t)gx +
-                             (uint32_t)x0;
-        // boundaries of the row's cells: e0 <= e1 <= e2 <= e3 (missing cells empty)
-        const uint32_t sv = cstart[row + min(lane & 3u, nc)];
-        const uint32_t e0 = __shfl_sync(kFull, sv, 0), e1 = __shfl_sync(kFull, sv, 1),
-                       e2 = __shfl_sync(kFull, sv, 2), e3 = __shfl_sync(kFull, sv, 3);
-        uint32_t c0 = 0, c1 = 0, c2 = 0;  // hits so far per cell of the row
-        uint32_t p = e0;
-        for (;;) {
-          // a cell that already holds S hits is done: skip to the next one
-          if (p < e1 && c0 >= S) p = e1;
-          if (p >= e1 && p < e2 && c1 >= S) p = e2;
-          if (p >= e2 && c2 >= S) p = e3;
-          if (p >= e3) break;
-          const uint32_t i = p + lane;
-          bool hit = false;
-          uint32_t gid = 0;
-          if (i < e3) {
-            const float4 v = pts[i];
-            const float dx = __fsub_rn(v.x, qx), dy = __fsub_rn(v.y, qy), dz = __fsub_rn(v.z, qz);
-            const float d2 =
-                __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
-            hit = d2 < r2;
-            gid = __float_as_uint(v.w);
-          }
-          const uint32_t k = (i >= e1 ? 1u : 0u) + (i >= e2 ? 1u : 0u);
-          const uint32_t m0 = __ballot_sync(kFull, hit && k == 0u);
-          const uint32_t m1 = __ballot_sync(kFull, hit && k == 1u);
-          const uint32_t m2 = __ballot_sync(kFull, hit && k == 2u);
-          const uint32_t before = k == 0u ? c0 + __popc(m0 & lt)
-                                          : (k == 1u ? c1 + __popc(m1 & lt) : c2 + __popc(m2 & lt));
-          if (hit && before < S) hits[((uint32_t)r * 3u + k) * S + before] = gid;
-          c0 += __popc(m0);
-          c1 += __popc(m1);
-          c2 += __popc(m2);
-          p += 32u;
-        }
-        if (lane == (uint32_t)r * 3u) cnt = min(c0, S);
-        if (lane == (uint32_t)r * 3u + 1u) cnt = min(c1, S);
-        if (lane == (uint32_t)r * 3u + 2u) cnt = min(c2, S);
+    // lane s < 27: neighbour cell (cx - 1 + s % 3, cy - 1 + s / 3 % 3, cz - 1 + s / 9)
+    uint32_t cb = 0, clen = 0;  // its first sorted position and point count
+    if (lane < 27u) {
+      const int x = cx - 1 + (int)(lane % 3u), y = cy - 1 + (int)(lane / 3u % 3u),
+                z = cz - 1 + (int)(lane / 9u);
+      if (x >= 0 && x < (int)gr.g[0] && y >= 0 && y < (int)gr.g[1] && z >= 0 &&
+          z < (int)gr.g[2]) {
+        const uint32_t cell =
+            gr.base + ((uint32_t)z * gr.g[1] + (uint32_t)y) * gr.g[0] + (uint32_t)x;
+        cb = cstart[cell];
+        clen = cstart[cell + 1] - cb;
       }
     }
+    uint32_t incl = clen;
+#pragma unroll
+    for (uint32_t o = 1; o < 32u; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t vs = incl - clen;  // start of cell `lane` in the concatenated range
+    const uint32_t L = __shfl_sync(kFull, incl, 31);
+    uint32_t cnt = 0;  // lane s: hits of cell s so far
+    for (uint32_t v0 = 0; v0 < L; v0 += 32u) {
+      const uint32_t v = v0 + lane;
+      const uint32_t s = last_le(vs, v);
+      const uint32_t sb = __shfl_sync(kFull, cb, s), svs = __shfl_sync(kFull, vs, s);
+      bool hit = false;
+      uint32_t gid = 0;
+      if (v < L) {
+        const float4 p = pts[sb + (v - svs)];
+        const float dx = __fsub_rn(p.x, qx), dy = __fsub_rn(p.y, qy), dz = __fsub_rn(p.z, qz);
+        const float d2 =
+            __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
+        hit = d2 < r2;
+        gid = __float_as_uint(p.w);
+      }
+      const uint32_t hm = __ballot_sync(kFull, hit);
+      if (hm) {
+        const uint32_t first_lane = svs > v0 ? svs - v0 : 0u;  // <= lane
+        const uint32_t before =
+            __shfl_sync(kFull, cnt, s) + __popc(hm & lt & ~lanes_below(first_lane));
+        if (hit && before < S) hits[s * S + before] = gid;
+        // lane s: this step's lanes [a, b) belong to cell s
+        const uint32_t a = min(max(vs, v0), v0 + 32u) - v0;
+        const uint32_t b = min(max(vs + clen, v0), v0 + 32u) - v0;
+        cnt += __popc(hm & lanes_below(b) & ~lanes_below(a));
+      }
+    }
+    const uint32_t kept = min(cnt, S);  // lanes >= 27 hold 0
+    uint32_t kincl = kept;
+#pragma unroll
+    for (uint32_t o = 1; o < 32u; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(kFull, kincl, o);
+      if (lane >= o) kincl += t;
+    }
+    const uint32_t kex = kincl - kept;
+    const uint32_t T = __shfl_sync(kFull, kincl, 31);  // ids kept over all cells
     __syncwarp();
-    // merge the sorted per-cell lists: the S smallest point ids, ascending
     const uint32_t pb = poff[c];
     const size_t ob = (size_t)j * S;
-    uint32_t ptr = 0;
-    uint32_t head = (lane < 27u && cnt > 0u) ? hits[lane * S] : kNone;
-    uint32_t first = kNone, mine = 0, t = 0;
-    for (; t < S; ++t) {
-      const uint32_t mn = __reduce_min_sync(kFull, head);
-      if (mn == kNone) break;
-      if (head == mn) {
-        ++ptr;
-        head = ptr < cnt ? hits[lane * S + ptr] : kNone;
+    if (T <= 32u) {
+      // lane i < T takes the i-th kept id; a bitonic sort orders them
+      const uint32_t s = last_le(kex, lane);
+      const uint32_t off = lane - __shfl_sync(kFull, kex, s);
+      uint32_t val = lane < T ? hits[s * S + off] : kNone;
+#pragma unroll
+      for (uint32_t k = 2; k <= 32u; k <<= 1)
+#pragma unroll
+        for (uint32_t jj = k >> 1; jj; jj >>= 1) {
+          const uint32_t other = __shfl_xor_sync(kFull, val, jj);
+          const bool up = (lane & k) == 0u, low = (lane & jj) == 0u;
+          val = (low == up) ? min(val, other) : max(val, other);
+        }
+      const uint32_t first = __shfl_sync(kFull, val, 0);
+      const uint32_t fill = T ? first : pb;
+      for (uint32_t q = lane; q < S; q += 32u)
+        out_idx[ob + q] = (int64_t)((q < T ? val : fill) - pb);
+    } else {
+      // merge the sorted per-cell lists: the S smallest ids, ascending
+      uint32_t ptr = 0;
+      uint32_t head = kept > 0u ? hits[lane * S] : kNone;
+      uint32_t first = kNone, mine = 0, t = 0;
+      for (; t < S; ++t) {
+        const uint32_t mn = __reduce_min_sync(kFull, head);
+        if (mn == kNone) break;
+        if (head == mn) {
+          ++ptr;
+          head = ptr < kept ? hits[lane * S + ptr] : kNone;
+        }
+        if (t == 0u) first = mn;
+        if ((t & 31u) == lane) mine = mn;
+        if ((t & 31u) == 31u) out_idx[ob + (t - 31u) + lane] = (int64_t)(mine - pb);
       }
-      if (t == 0u) first = mn;
-      if ((t & 31u) == lane) mine = mn;
-      if ((t & 31u) == 31u) out_idx[ob + (t - 31u) + lane] = (int64_t)(mine - pb);
+      for (uint32_t q = (t & ~31u) + lane; q < S; q += 32u)
+        out_idx[ob + q] = (int64_t)((q < t ? mine : first) - pb);
     }
-    // the rest of the last chunk, then padding with the first hit (or 0)
-    const uint32_t fill = t == 0u ? pb : first;
-    for (uint32_t q = (t & ~31u) + lane; q < S; q += 32u)
-      out_idx[ob + q] = (int64_t)((q < t ? mine : fill) - pb);
-    if (lane == 0 && out_hits) out_hits[j] = t;
+    if (lane == 0 && out_hits) out_hits[j] = min(T, S);
     __syncwarp();  // the hit lists are rewritten for the next centre
   }
 }

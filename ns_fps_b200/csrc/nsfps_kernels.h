@@ -44,7 +44,7 @@ struct SetupArgs {
   const RangeDev *ranges;
   const uint32_t *boff;       // B bucket offsets
   uint32_t *keys0, *vals0, *keys1, *vals1;  // n each
-  uint32_t *hist;             // 256 * ceil(n / 4096)
+  uint32_t *hist;             // 256 * radix_tiles(n) + 1
   uint32_t *partial;          // ceil(max scan length / 4096) + 2
   float4 *pts;                // n sorted (x, y, z, dist)
   uint32_t *perm;             // n sorted -> input point id
@@ -63,10 +63,12 @@ struct SetupArgs {
 
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches);
 
+// Tiles the radix sort splits n keys into.
+uint32_t radix_tiles(uint32_t n);
 // Stable LSD radix sort of n (key, value) pairs, 8-bit digits over the bits of
 // max_key.  *keys / *vals hold the input and, on return, point at whichever of
-// the two buffer pairs holds the sorted result.  hist: 256 * ceil(n / 4096)
-// + 1 entries; partial: ceil(256 * ceil(n / 4096) / 4096) + 2.
+// the two buffer pairs holds the sorted result.  hist: 256 * radix_tiles(n)
+// + 1 entries; partial: ceil(256 * radix_tiles(n) / 4096) + 2.
 cudaError_t run_sort_pairs(uint32_t **keys, uint32_t **vals, uint32_t *keys_alt,
                            uint32_t *vals_alt, uint32_t n, uint32_t max_key, uint32_t *hist,
                            uint32_t *partial, cudaStream_t st, uint32_t &launches);

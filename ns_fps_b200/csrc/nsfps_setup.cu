@@ -150,18 +150,23 @@ void device_scan(const uint32_t *in, uint32_t *out, uint32_t n,
 }
 
 // ------------------------------------------------------------- radix sort
+// Tiles of 8 warps x R rounds x 32 lanes keys: R = 16 (4096 keys) for large
+// inputs, R = 4 (1024 keys) below kSmallSortKeys so that small sorts still
+// spread over the SMs.
 constexpr int kRsThreads = 256;
-constexpr int kRsTile = 4096;  // 8 warps x 16 rounds x 32 lanes
+constexpr uint32_t kSmallSortKeys = 1u << 19;
 
+template <int R>
 __global__ void __launch_bounds__(kRsThreads)
 radix_upsweep(const uint32_t *__restrict__ kin, uint32_t n, int shift,
               uint32_t *__restrict__ hist, uint32_t ntiles) {
+  constexpr int kTile = 8 * R * 32;
   __shared__ uint32_t cnt[256];
   cnt[threadIdx.x] = 0;
   __syncthreads();
-  const uint64_t base = (uint64_t)blockIdx.x * kRsTile;
+  const uint64_t base = (uint64_t)blockIdx.x * kTile;
 #pragma unroll 4
-  for (int r = 0; r < kRsTile / kRsThreads; ++r) {
+  for (int r = 0; r < kTile / kRsThreads; ++r) {
     const uint64_t idx = base + r * kRsThreads + threadIdx.x;
     if (idx < n) atomicAdd(&cnt[(kin[idx] >> shift) & 255u], 1u);
   }
@@ -169,22 +174,24 @@ radix_upsweep(const uint32_t *__restrict__ kin, uint32_t n, int shift,
   hist[(uint64_t)threadIdx.x * ntiles + blockIdx.x] = cnt[threadIdx.x];
 }
 
-// Stable scatter: warp w of a tile owns keys [w*512, w*512+512) of the tile in
-// 16 ordered rounds of 32; ranks inside a round come from __match_any_sync.
+// Stable scatter: warp w of a tile owns keys [w*R*32, (w+1)*R*32) of the tile
+// in R ordered rounds of 32; ranks inside a round come from __match_any_sync.
+template <int R>
 __global__ void __launch_bounds__(kRsThreads)
 radix_downsweep(const uint32_t *__restrict__ kin,
                 const uint32_t *__restrict__ vin, uint32_t *__restrict__ kout,
                 uint32_t *__restrict__ vout, uint32_t n, int shift,
                 const uint32_t *__restrict__ hist, uint32_t ntiles) {
+  constexpr int kTile = 8 * R * 32;
   __shared__ uint32_t wcount[8][256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < 8 * 256; i += kRsThreads) (&wcount[0][0])[i] = 0;
   __syncthreads();
-  const uint64_t base = (uint64_t)blockIdx.x * kRsTile + warp * 512;
+  const uint64_t base = (uint64_t)blockIdx.x * kTile + warp * (R * 32);
   const uint32_t lt = (1u << lane) - 1u;
-  uint32_t key[16], val[16];
+  uint32_t key[R], val[R];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
+  for (int r = 0; r < R; ++r) {
     const uint64_t idx = base + r * 32 + lane;
     const bool valid = idx < n;
     key[r] = valid ? kin[idx] : 0u;
@@ -207,7 +214,7 @@ radix_downsweep(const uint32_t *__restrict__ kin,
   }
   __syncthreads();
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
+  for (int r = 0; r < R; ++r) {
     const uint64_t idx = base + r * 32 + lane;
     const bool valid = idx < n;
     const uint32_t d = valid ? ((key[r] >> shift) & 255u) : (256u + lane);
@@ -467,6 +474,10 @@ cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, f
   return cudaGetLastError();
 }
 
+uint32_t radix_tiles(uint32_t n) {
+  return n < kSmallSortKeys ? cdiv(n, 8 * 4 * 32) : cdiv(n, 8 * 16 * 32);
+}
+
 cudaError_t run_sort_pairs(uint32_t **keys, uint32_t **vals, uint32_t *keys_alt,
                            uint32_t *vals_alt, uint32_t n, uint32_t max_key, uint32_t *hist,
                            uint32_t *partial, cudaStream_t st, uint32_t &launches) {
@@ -475,13 +486,21 @@ cudaError_t run_sort_pairs(uint32_t **keys, uint32_t **vals, uint32_t *keys_alt,
   while (bits < 32 && ((max_key >> bits) != 0)) ++bits;
   const int passes = (bits + 7) / 8;
   uint32_t *kin = *keys, *vin = *vals, *kout = keys_alt, *vout = vals_alt;
-  const uint32_t ntiles = cdiv(n, kRsTile);
+  const bool small = n < kSmallSortKeys;
+  const uint32_t ntiles = radix_tiles(n);
   for (int pass = 0; pass < passes; ++pass) {
     const int shift = pass * 8;
-    radix_upsweep<<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, hist, ntiles);
+    if (small)
+      radix_upsweep<4><<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, hist, ntiles);
+    else
+      radix_upsweep<16><<<ntiles, kRsThreads, 0, st>>>(kin, n, shift, hist, ntiles);
     device_scan<false, false>(hist, hist, 256u * ntiles, partial, st, launches);
-    radix_downsweep<<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift, hist,
-                                                   ntiles);
+    if (small)
+      radix_downsweep<4><<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift, hist,
+                                                        ntiles);
+    else
+      radix_downsweep<16><<<ntiles, kRsThreads, 0, st>>>(kin, vin, kout, vout, n, shift, hist,
+                                                         ntiles);
     launches += 2;
     uint32_t *t;
     t = kin; kin = kout; kout = t;
