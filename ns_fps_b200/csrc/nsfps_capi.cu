@@ -667,7 +667,9 @@ int device_bboxes(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz, const uin
   uint32_t launches = 0;
   NSFPS_CUDA(cudaMemcpyAsync(d_poff, hpoff.data(), sizeof(uint32_t) * (count + 1),
                              cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(run_cloud_bbox(d_xyz, d_poff, (uint32_t)count, d_box, st, launches));
+  uint32_t max_cloud = 0;
+  for (uint64_t i = 0; i < count; ++i) max_cloud = std::max(max_cloud, hpoff[i + 1] - hpoff[i]);
+  NSFPS_CUDA(run_cloud_bbox(d_xyz, d_poff, (uint32_t)count, max_cloud, d_box, st, launches));
   NSFPS_CUDA(cudaMemcpyAsync(hbox.data(), d_box, sizeof(float) * 6 * count,
                              cudaMemcpyDeviceToHost, st));
   NSFPS_CUDA(cudaStreamSynchronize(st));

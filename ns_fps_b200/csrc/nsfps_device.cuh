@@ -129,6 +129,13 @@ __device__ __forceinline__ void st_release_cta_if(bool pred, uint32_t *p, uint32
 }
 
 // Acquire load of a global word, GPU scope.
+// Release add at GPU scope: the writes this thread has observed (its own,
+// and those of threads it synchronised with, e.g. through __syncwarp) are
+// visible to any thread that reads the new value with acquire semantics.
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -78,9 +78,10 @@ cudaError_t run_exclusive_scan(const uint32_t *in, uint32_t *out, uint32_t n,
                                uint32_t *partial, cudaStream_t st, uint32_t &launches);
 
 // compute_bbox of each of B device-resident clouds (poff: B + 1 point
-// offsets, device): out[6c .. 6c+5] = min x, y, z, max x, y, z.
-cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, float *out,
-                           cudaStream_t st, uint32_t &launches);
+// offsets, device; max_cloud: points of the largest): out[6c .. 6c+5] =
+// min x, y, z, max x, y, z.
+cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B,
+                           uint32_t max_cloud, float *out, cudaStream_t st, uint32_t &launches);
 
 struct LoopArgs {
   uint32_t B;                 // clouds in this launch

@@ -660,11 +660,10 @@ fps_rounds_cluster(const LoopArgs a) {
           const uint4 *src = reinterpret_cast<const uint4 *>(&ctl.stage);
           uint4 *dst = a.glist + ((size_t)(round & 1u) * P + crank) * kWords;
           for (int w = lane; w < kWords; w += 32) __stcg(dst + w, src[w]);
-          __threadfence();
-          __syncwarp();
+          __syncwarp();  // lane 0's release below covers every lane's stores
           if (lane == 0) {
             const uint32_t target = (round + 1u) * P;
-            atomicAdd(a.gbar, 1u);
+            red_release_gpu_add(a.gbar, 1u);
             unsigned long long deadline = 0;
             uint32_t polls = 0;
             while (ld_acquire_gpu(a.gbar) < target) {

@@ -20,6 +20,7 @@
 //                        shared memory.
 //
 // Everything here is O(N) memory; no array is sized by the number of buckets.
+#include <algorithm>
 #include <cfloat>
 
 #include "nsfps_internal.cuh"
@@ -407,57 +408,82 @@ __global__ void plan_partition(const float4 *__restrict__ leaf_lo,
 // compute_bbox (src/yuezu_fps.cpp:648-670) of each cloud, on the device: the
 // per-axis minimum and maximum of the cloud's points.  The reference scans
 // from point 0 with `v < min` / `max < v`, which never take a NaN, so a NaN
-// survives only as point 0's own coordinate; fminf/fmaxf skip NaNs the same
-// way elsewhere.  (Signed zeros can differ in which zero wins, which the
-// +-BOUNDARY_EPS applied afterwards makes irrelevant.)  One block per cloud.
+// survives only as point 0's own coordinate; elsewhere NaNs are skipped.
+// (Signed zeros can differ in which zero wins, which the +-BOUNDARY_EPS
+// applied afterwards makes irrelevant.)
+//
+// Three launches: bbox_init sets the per-cloud extremes to their identities,
+// cloud_bbox reduces slices of every cloud (grid x = slices, y = clouds) and
+// merges them with integer atomics on order-preserving encodings of the
+// floats, and bbox_final decodes them in place and applies point 0's NaNs.
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float ordered_float(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+__global__ void bbox_init(uint32_t *__restrict__ enc, uint32_t B) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= B) return;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    enc[6 * (size_t)c + a] = 0xffffffffu;
+    enc[6 * (size_t)c + 3 + a] = 0u;
+  }
+}
+
 __global__ void __launch_bounds__(256)
 cloud_bbox(const float *__restrict__ xyz, const uint32_t *__restrict__ poff, uint32_t B,
-           float *__restrict__ out) {
-  const uint32_t c = blockIdx.x;
+           uint32_t *__restrict__ enc) {
+  for (uint32_t c = blockIdx.y; c < B; c += gridDim.y) {
+    const uint32_t s = poff[c], e = poff[c + 1];
+    const uint32_t per = (e - s + gridDim.x - 1) / gridDim.x;
+    const uint32_t b0 = s + blockIdx.x * per, b1 = min(e, b0 + per);
+    uint32_t mn[3] = {0xffffffffu, 0xffffffffu, 0xffffffffu}, mx[3] = {0u, 0u, 0u};
+    for (uint32_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) {
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const float v = xyz[3 * (size_t)i + a];
+        if (v != v) continue;
+        const uint32_t o = ordered_bits(v);
+        mn[a] = min(mn[a], o);
+        mx[a] = max(mx[a], o);
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      mn[a] = __reduce_min_sync(0xffffffffu, mn[a]);
+      mx[a] = __reduce_max_sync(0xffffffffu, mx[a]);
+    }
+    if ((threadIdx.x & 31u) == 0)
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        if (mn[a] != 0xffffffffu) atomicMin(&enc[6 * (size_t)c + a], mn[a]);
+        if (mx[a] != 0u) atomicMax(&enc[6 * (size_t)c + 3 + a], mx[a]);
+      }
+  }
+}
+
+__global__ void bbox_final(const float *__restrict__ xyz, const uint32_t *__restrict__ poff,
+                           uint32_t B, uint32_t *__restrict__ enc) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= B) return;
   const uint32_t s = poff[c], e = poff[c + 1];
   const float inf = __int_as_float(0x7f800000);
-  float mn[3] = {inf, inf, inf}, mx[3] = {-inf, -inf, -inf};
-  for (uint32_t i = s + threadIdx.x; i < e; i += blockDim.x) {
+  float *out = reinterpret_cast<float *>(enc);
 #pragma unroll
-    for (int a = 0; a < 3; ++a) {
-      const float v = xyz[3 * (size_t)i + a];
-      mn[a] = fminf(mn[a], v);
-      mx[a] = fmaxf(mx[a], v);
+  for (int a = 0; a < 3; ++a) {
+    const uint32_t omn = enc[6 * (size_t)c + a], omx = enc[6 * (size_t)c + 3 + a];
+    float lo = omn == 0xffffffffu ? inf : ordered_float(omn);
+    float hi = omx == 0u ? -inf : ordered_float(omx);
+    if (e > s) {  // point 0 starts the scan: a NaN there is kept
+      const float v0 = xyz[3 * (size_t)s + a];
+      if (v0 != v0) lo = hi = v0;
     }
-  }
-  __shared__ float red[6][8];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      mn[a] = fminf(mn[a], __shfl_xor_sync(0xffffffffu, mn[a], o));
-      mx[a] = fmaxf(mx[a], __shfl_xor_sync(0xffffffffu, mx[a], o));
-    }
-  if (lane == 0) {
-#pragma unroll
-    for (int a = 0; a < 3; ++a) { red[a][warp] = mn[a]; red[3 + a][warp] = mx[a]; }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int nw = (int)(blockDim.x >> 5);
-    for (int w = 1; w < nw; ++w)
-#pragma unroll
-      for (int a = 0; a < 3; ++a) {
-        red[a][0] = fminf(red[a][0], red[a][w]);
-        red[3 + a][0] = fmaxf(red[3 + a][0], red[3 + a][w]);
-      }
-#pragma unroll
-    for (int a = 0; a < 3; ++a) {
-      float lo = red[a][0], hi = red[3 + a][0];
-      if (e > s) {  // point 0 starts the scan: a NaN there is kept
-        const float v0 = xyz[3 * (size_t)s + a];
-        if (v0 != v0) lo = hi = v0;
-      }
-      out[6 * (size_t)c + a] = lo;
-      out[6 * (size_t)c + 3 + a] = hi;
-    }
+    out[6 * (size_t)c + a] = lo;
+    out[6 * (size_t)c + 3 + a] = hi;
   }
 }
 
@@ -466,11 +492,15 @@ inline uint32_t cdiv(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b
 }  // namespace
 
 // ------------------------------------------------------------------ driver
-cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B, float *out,
-                           cudaStream_t st, uint32_t &launches) {
+cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B,
+                           uint32_t max_cloud, float *out, cudaStream_t st, uint32_t &launches) {
   if (B == 0) return cudaSuccess;
-  cloud_bbox<<<B, 256, 0, st>>>(xyz, poff, B, out);
-  launches += 1;
+  uint32_t *enc = reinterpret_cast<uint32_t *>(out);
+  const uint32_t slices = std::max(1u, std::min(cdiv(max_cloud, 2048), 1024u));
+  bbox_init<<<cdiv(B, 128), 128, 0, st>>>(enc, B);
+  cloud_bbox<<<dim3(slices, std::min(B, 65535u)), 256, 0, st>>>(xyz, poff, B, enc);
+  bbox_final<<<cdiv(B, 128), 128, 0, st>>>(xyz, poff, B, enc);
+  launches += 3;
   return cudaGetLastError();
 }
 
