@@ -128,7 +128,6 @@ __device__ __forceinline__ void st_release_cta_if(bool pred, uint32_t *p, uint32
       : "memory");
 }
 
-// Acquire load of a global word, GPU scope.
 // Release add at GPU scope: the writes this thread has observed (its own,
 // and those of threads it synchronised with, e.g. through __syncwarp) are
 // visible to any thread that reads the new value with acquire semantics.
@@ -136,6 +135,7 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Acquire load of a global word, GPU scope.
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -146,6 +146,39 @@ __device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
   return v;
+}
+
+// Two fp32 lanes in one 64-bit register (element 0 in the low word).
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2unpack(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+// Squared distances of two points (packed x, y, z pairs) to one point q (each
+// coordinate duplicated into both lanes) with the sm_100 packed fp32
+// instructions: per lane exactly sqdist()'s ((dx*dx + dy*dy) + dz*dz), every
+// operation IEEE round-to-nearest, no contraction.
+__device__ __forceinline__ unsigned long long sqdist_x2(unsigned long long px, unsigned long long py,
+                                                        unsigned long long pz, unsigned long long qx,
+                                                        unsigned long long qy, unsigned long long qz) {
+  unsigned long long r;
+  asm("{\n\t.reg .b64 dx, dy, dz;\n\t"
+      "sub.rn.f32x2 dx, %1, %4;\n\t"
+      "sub.rn.f32x2 dy, %2, %5;\n\t"
+      "sub.rn.f32x2 dz, %3, %6;\n\t"
+      "mul.rn.f32x2 dx, dx, dx;\n\t"
+      "mul.rn.f32x2 dy, dy, dy;\n\t"
+      "mul.rn.f32x2 dz, dz, dz;\n\t"
+      "add.rn.f32x2 dx, dx, dy;\n\t"
+      "add.rn.f32x2 %0, dx, dz;\n\t}"
+      : "=l"(r)
+      : "l"(px), "l"(py), "l"(pz), "l"(qx), "l"(qy), "l"(qz));
+  return r;
 }
 
 __device__ __forceinline__ float sqrt_approx(float x) {

@@ -758,6 +758,16 @@ fps_rounds_cluster(const LoopArgs a) {
           }
         }
         const uint32_t rows = (L + 32u * kReplay - 1u) / (32u * kReplay);
+        // candidate pairs (rows 2h, 2h + 1) packed for the f32x2 distances
+        constexpr int kPairs = kCandPerLane / 2 > 0 ? kCandPerLane / 2 : 1;
+        unsigned long long px2[kPairs], py2[kPairs], pz2[kPairs];
+#pragma unroll
+        for (int h = 0; h < kPairs; ++h) {
+          const int c0 = 2 * h, c1 = 2 * h + 1 < kCandPerLane ? 2 * h + 1 : 2 * h;
+          px2[h] = f2pack(cx[c0], cx[c1]);
+          py2[h] = f2pack(cy[c0], cy[c1]);
+          pz2[h] = f2pack(cz[c0], cz[c1]);
+        }
 
         // Each iteration takes the kSpec best candidates W0 > W1 > ... and
         // decides the longest prefix of them that are the reference's next
@@ -901,9 +911,23 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
             for (int j = 0; j < kSpec; ++j)
               if ((uint32_t)j < m) {
+                // the candidates' distances to the sample, two at a time
+                // (sm_100 f32x2, bit-identical to sqdist())
+                float pd[R];
+                if (R >= 2) {
+                  const unsigned long long qx2 = f2pack(wx[j], wx[j]), qy2 = f2pack(wy[j], wy[j]),
+                                           qz2 = f2pack(wz[j], wz[j]);
+#pragma unroll
+                  for (int h = 0; h < R / 2; ++h)
+                    f2unpack(sqdist_x2(px2[h], py2[h], pz2[h], qx2, qy2, qz2), pd[2 * h],
+                             pd[2 * h + 1]);
+                } else {
+                  pd[0] = sqdist(cx[0], cy[0], cz[0], wx[j], wy[j], wz[j]);
+                }
 #pragma unroll
                 for (int c = 0; c < R; ++c) {  // branch-free per candidate
-                  const uint32_t dk = dkey(sqdist(cx[c], cy[c], cz[c], wx[j], wy[j], wz[j]));
+                  // distances are never negative: the key is the bits + 1
+                  const uint32_t dk = __float_as_uint(pd[c]) + 1u;
                   const bool in = (gx[c] - (wcube[j][0] & 0xffffu)) <= (wcube[j][0] >> 16) &&
                                   (gy[c] - (wcube[j][1] & 0xffffu)) <= (wcube[j][1] >> 16) &&
                                   (gz[c] - (wcube[j][2] & 0xffffu)) <= (wcube[j][2] >> 16);
