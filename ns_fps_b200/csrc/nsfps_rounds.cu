@@ -80,14 +80,14 @@ __device__ __forceinline__ int worker_index(int warp) {
 #define NSFPS_ROUND_T 8
 #endif
 constexpr int kRoundT = NSFPS_ROUND_T;
-constexpr int kMaxCands = kRoundT * 16 > 256 ? kRoundT * 16 : 256;  // P * T
-static_assert(kMaxCands <= 512, "at most 512 candidates (9-bit slots)");
+// Candidates per round, at most (P * T): the kernel's template parameter CAP,
+// 256 in a cluster and in the 64-CTA grid, 512 in the 128-CTA grid.
+constexpr int kClusterCap = kRoundT * 16 > 256 ? kRoundT * 16 : 256;
 // Received lists rotate over two buffers: a CTA publishes round r+2 only
 // after it has every round r+1 list, so after every CTA compacted round r.
 constexpr int kListBufs = 2;
-// Bits of the candidate slot in a replay key.
-constexpr int kSlotBits = kMaxCands > 256 ? 9 : 8;
-constexpr int kCandPerLane = kMaxCands / (32 * kReplay);
+// Bits of the candidate slot in a replay key, for a capacity.
+__host__ __device__ constexpr int cap_slot_bits(int cap) { return cap > 256 ? 9 : 8; }
 constexpr int kQueue = 512;                    // samples decided per round, at most
 constexpr int kBatch = 1;                      // samples a worker applies together
 // Steps decided per replay iteration, at most (see the replay loop).
@@ -118,11 +118,11 @@ struct __align__(16) CtaList {
   unsigned long long pad;
 };
 
-template <int T>
+template <int T, int CAP>
 struct RoundCtl {
   CtaList<T> list[kListBufs][kMaxClusterP];  // received lists, by source CTA
   CtaList<T> stage;                      // this CTA's list, copied out from here
-  Cand live[kMaxCands];                  // the round's candidates that beat B*
+  Cand live[CAP];                        // the round's candidates that beat B*
   uint32_t nlive[kReplay];
   unsigned long long mbar[kListBufs];
   unsigned long long wkey[kWarps][T + 1];   // per-warp best leaves
@@ -206,19 +206,24 @@ __device__ __forceinline__ void replay_sync() {
 // winner's slot and position read straight out of the key.  One cloud spans
 // at most 128 CTAs of fewer than 65536 points, so the position fits in
 // 32 - S >= 23 bits.
+template <int S>
 __device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
-  return ((((1u << (32 - kSlotBits)) - 1u) - rel_pos) << kSlotBits) | slot;
+  return ((((1u << (32 - S)) - 1u) - rel_pos) << S) | slot;
 }
 
 // GRID: the cloud's P CTAs are co-resident but not one cluster; the lists go
 // through global memory (a.glist, by round parity) and a grid barrier (a.gbar)
 // replaces the cluster copies and mbarriers.
-template <int M, int T, bool GRID>
+template <int M, int T, bool GRID, int CAP>
 __global__ void __launch_bounds__(kRoundThreads, 1)
 fps_rounds_cluster(const LoopArgs a) {
   constexpr int THREADS = kRoundThreads;
+  constexpr int kMaxCands = CAP;
+  static_assert(kMaxCands <= 512, "at most 512 candidates (9-bit slots)");
+  constexpr int kSlotBits = cap_slot_bits(CAP);
+  constexpr int kCandPerLane = kMaxCands / (32 * kReplay);
   extern __shared__ float4 smem[];
-  __shared__ RoundCtl<T> ctl;
+  __shared__ RoundCtl<T, CAP> ctl;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t P = a.P;
@@ -704,7 +709,7 @@ fps_rounds_cluster(const LoopArgs a) {
         for (uint32_t i = (uint32_t)lane; i < P; i += 32u) {
           unsigned long long b = GRID ? __ldcg(&lists[i].bound) : lists[i].bound;
           if (b != 0ull)
-            b = (b & 0xffffffff00000000ull) | replay_lo((0xffffffffu - (uint32_t)b) - pbase, 0u);
+            b = (b & 0xffffffff00000000ull) | replay_lo<kSlotBits>((0xffffffffu - (uint32_t)b) - pbase, 0u);
           bl = max64(bl, b);
         }
         const unsigned long long bstar = warp_max64_key(bl);
@@ -715,7 +720,7 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
         for (int c = 0; c < kCandPerLane; ++c) {
           lv[c] = lc[c].d >= 0.0f &&
-                  (((unsigned long long)dkey(lc[c].d) << 32) | replay_lo(lc[c].pos - pbase, 0u)) > bstar;
+                  (((unsigned long long)dkey(lc[c].d) << 32) | replay_lo<kSlotBits>(lc[c].pos - pbase, 0u)) > bstar;
           const uint32_t bm = __ballot_sync(kFull, lv[c]);
           lslot[c] = nl_w + __popc(bm & lanemask_lt());
           nl_w += __popc(bm);
@@ -753,7 +758,7 @@ fps_rounds_cluster(const LoopArgs a) {
             const Cand cd = ctl.live[idx];
             cx[c] = cd.x; cy[c] = cd.y; cz[c] = cd.z;
             ck[c] = dkey(cd.d);
-            clo[c] = replay_lo(cd.pos - pbase, idx);
+            clo[c] = replay_lo<kSlotBits>(cd.pos - pbase, idx);
             gx[c] = cd.cell & 1023u; gy[c] = (cd.cell >> 10) & 1023u; gz[c] = cd.cell >> 20;
           }
         }
@@ -1025,9 +1030,9 @@ fps_rounds_cluster(const LoopArgs a) {
   // remote write of that round was awaited, so no final cluster barrier.
 }
 
-template <int M, int T, bool GRID>
+template <int M, int T, bool GRID, int CAP>
 cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
-  auto kern = fps_rounds_cluster<M, T, GRID>;
+  auto kern = fps_rounds_cluster<M, T, GRID, CAP>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err) return err;
@@ -1055,26 +1060,30 @@ cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int T, bool GRID>
+template <int T, bool GRID, int CAP>
 cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t st) {
   switch (m) {
-    case 1: return launch_rounds<1, T, GRID>(a, smem, st);
-    case 2: return launch_rounds<2, T, GRID>(a, smem, st);
-    case 3: return launch_rounds<3, T, GRID>(a, smem, st);
-    case 4: return launch_rounds<4, T, GRID>(a, smem, st);
+    case 1: return launch_rounds<1, T, GRID, CAP>(a, smem, st);
+    case 2: return launch_rounds<2, T, GRID, CAP>(a, smem, st);
+    case 3: return launch_rounds<3, T, GRID, CAP>(a, smem, st);
+    case 4: return launch_rounds<4, T, GRID, CAP>(a, smem, st);
     case 6: return kMaxLeavesPerThread >= 6
-                       ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T, GRID>(a, smem, st)
+                       ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T, GRID, CAP>(a, smem, st)
                        : cudaErrorInvalidValue;
     case 8: return kMaxLeavesPerThread >= 8
-                       ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T, GRID>(a, smem, st)
+                       ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T, GRID, CAP>(a, smem, st)
                        : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
 
-// Grid-wide rounds over P = 64 or 128 CTAs publish 256 / P candidates per
-// CTA (256 in all, as a full cluster does).
-constexpr int grid_t(uint32_t P) { return P == 64u ? 4 : (P == 128u ? 2 : 0); }
+// Grid-wide rounds over P = 64 or 128 CTAs publish 4 candidates per CTA
+// (256 or 512 in all).  The round lasts while the best candidate beats the
+// largest CTA bound; more candidates per CTA lower that bound but cost
+// every step more work: on c2 (P = 64) 8 per CTA gave 4.19 ms against 4.16
+// for 4, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
+constexpr int grid_t(uint32_t P) { return P == 64u ? 4 : (P == 128u ? 4 : 0); }
+constexpr int grid_cap(uint32_t P) { return (int)P * grid_t(P); }
 
 }  // namespace
 
@@ -1098,9 +1107,9 @@ int rounds_max_smem(uint32_t P) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   // the grid-wide loop (P > one cluster) keeps smaller lists in shared memory
-  const int ctl = P == 64u    ? (int)sizeof(RoundCtl<grid_t(64)>)
-                  : P == 128u ? (int)sizeof(RoundCtl<grid_t(128)>)
-                              : (int)sizeof(RoundCtl<kRoundT>);
+  const int ctl = P == 64u    ? (int)sizeof(RoundCtl<grid_t(64), grid_cap(64)>)
+                  : P == 128u ? (int)sizeof(RoundCtl<grid_t(128), grid_cap(128)>)
+                              : (int)sizeof(RoundCtl<kRoundT, kClusterCap>);
   return optin - ctl - 1024;
 }
 
@@ -1121,11 +1130,13 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
     if (a.B != 1 || !a.glist || !a.gbar || rounds_grid_candidates_per_cta(a.P) == 0)
       return cudaErrorInvalidValue;
     if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t), st))) return err;
-    err = a.P == 64u ? launch_rounds_m<grid_t(64), true>(a, plan.leaves_per_thread, plan.smem_bytes, st)
-                     : launch_rounds_m<grid_t(128), true>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+    err = a.P == 64u ? launch_rounds_m<grid_t(64), true, grid_cap(64)>(a, plan.leaves_per_thread,
+                                                                         plan.smem_bytes, st)
+                     : launch_rounds_m<grid_t(128), true, grid_cap(128)>(a, plan.leaves_per_thread,
+                                                                           plan.smem_bytes, st);
   } else {
     if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
-    err = launch_rounds_m<kRoundT, false>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+    err = launch_rounds_m<kRoundT, false, kClusterCap>(a, plan.leaves_per_thread, plan.smem_bytes, st);
   }
   launches += 1;
   return err;
