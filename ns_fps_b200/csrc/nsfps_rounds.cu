@@ -926,6 +926,8 @@ fps_rounds_cluster(const LoopArgs a) {
                   for (int h = 0; h < R / 2; ++h)
                     f2unpack(sqdist_x2(px2[h], py2[h], pz2[h], qx2, qy2, qz2), pd[2 * h],
                              pd[2 * h + 1]);
+                  if (R & 1)  // an odd last row
+                    pd[R - 1] = sqdist(cx[R - 1], cy[R - 1], cz[R - 1], wx[j], wy[j], wz[j]);
                 } else {
                   pd[0] = sqdist(cx[0], cy[0], cz[0], wx[j], wy[j], wz[j]);
                 }
@@ -1077,12 +1079,12 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
   }
 }
 
-// Grid-wide rounds over P = 64 or 128 CTAs publish 4 candidates per CTA
-// (256 or 512 in all).  The round lasts while the best candidate beats the
-// largest CTA bound; more candidates per CTA lower that bound but cost
-// every step more work: on c2 (P = 64) 8 per CTA gave 4.19 ms against 4.16
-// for 4, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
-constexpr int grid_t(uint32_t P) { return P == 64u ? 4 : (P == 128u ? 4 : 0); }
+// Grid-wide rounds over P = 64 or 128 CTAs publish 6 or 4 candidates per
+// CTA (384 or 512 in all).  The round lasts while the best candidate beats
+// the largest CTA bound; more candidates per CTA lower that bound but cost
+// every step more work: on c2 (P = 64) 4, 6 and 8 per CTA gave 4.160, 4.149
+// and 4.19 ms, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
+constexpr int grid_t(uint32_t P) { return P == 64u ? 6 : (P == 128u ? 4 : 0); }
 constexpr int grid_cap(uint32_t P) { return (int)P * grid_t(P); }
 
 }  // namespace
