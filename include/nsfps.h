@@ -253,8 +253,8 @@ NSFPS_API int nsfps_group_points_device(const float *d_xyz, const uint64_t *poin
  * (summed over iterations), points actually re-evaluated after the exact
  * bounding-box skip, and the loop configuration (CTAs per cloud and mode:
  * 0 = per-step cluster loop, 2 = round-based cluster loop, 3 = round-based
- * loop over co-resident CTAs for one cloud larger than a cluster's shared
- * memory).  After a ball query (mode 4): setup = the grid build, loop = the
+ * loop over 64 or 128 co-resident CTAs for one cloud of at least 98,304
+ * points or larger than a cluster's shared memory).  After a ball query (mode 4): setup = the grid build, loop = the
  * query kernel, launches = its kernel launches; the work counters are 0.
  * Enabled by nsfps_set_profiling. */
 typedef struct nsfps_profile {

@@ -1,0 +1,75 @@
+"""GPU parity of the grid-wide round loop (one cloud of at least 98,304 points
+spread over 64 or 128 co-resident CTAs, 384 or 512 published candidates per
+round) on seeded random clouds, against the CPU oracle: bit-exact indices.
+
+The golden vectors pin this path on the c2 and c4 configs only; these cases
+add exact distance ties (quantised coordinates), clamped outliers (ranges
+narrower than the data), clustered and flat clouds, and several direct
+(power-of-two) grids, and check that the grid-wide loop is what ran.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from tests import capi
+
+pytestmark = pytest.mark.gpu
+
+MODE_GRID = 3  # nsfps_profile.mode of the grid-wide round loop
+
+
+def _cloud(rs, n, kind):
+    if kind == 0:    # quantised: many exact ties among distances
+        return (np.round(rs.randn(n, 3) * 8) / 4).astype(np.float32)
+    if kind == 1:    # clustered
+        c = rs.randn(24, 3) * 40
+        return (c[rs.randint(0, 24, n)] + rs.randn(n, 3) * rs.uniform(0.5, 3)).astype(np.float32)
+    if kind == 2:    # flat, scan-like
+        p = rs.rand(n, 3) * [120, 120, 4]
+        return p.astype(np.float32)
+    return rs.randn(n, 3).astype(np.float32)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_grid_loop_random_clouds_match_oracle(seed):
+    rs = np.random.RandomState(7000 + seed)
+    n = int(rs.choice([100_000, 160_000, 260_000]))
+    pts = _cloud(rs, n, seed % 4)
+    blocks = tuple(int(v) for v in rs.choice([8, 16, 32, 64], 3))
+    lo, hi = pts.min(0), pts.max(0)
+    shrink = rs.uniform(0.75, 1.05)  # below 1: points outside the range are clamped
+    mid, half = (lo + hi) / 2, (hi - lo) / 2 * shrink + 1e-3
+    bounds = (mid[0] - half[0], mid[0] + half[0], mid[1] - half[1], mid[1] + half[1],
+              mid[2] - half[2], mid[2] + half[2])
+    k = int(rs.choice([2_000, 6_000]))
+    exp = oracle.fps(pts, k, bounds, blocks)
+    capi.set_profiling(True)
+    try:
+        got = capi.fps(pts, k, bounds, blocks)
+        prof = capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+    assert prof.mode == MODE_GRID, f"expected the grid-wide loop, ran mode {prof.mode}"
+    assert prof.ctas_per_cloud in (64, 128)
+    assert np.array_equal(got, exp), (
+        f"n={n} k={k} blocks={blocks}: first mismatch at "
+        f"{np.nonzero(got[:len(exp)] != exp[:len(got)])[0][:5]}")
+
+
+def test_grid_loop_work_counter_equals_reference_work():
+    """On a c2 scan (the grid-wide loop over 64 CTAs) the kernel's count of
+    points in the buckets the reference updates equals the oracle's."""
+    from ns_fps_b200 import synthetic as S
+    cfg = S.CONFIGS["c2"]
+    pts = S.make("c2", seed=11, count=1)[0]
+    capi.set_profiling(True)
+    try:
+        idx = capi.fps(pts, cfg.k, cfg.rng, cfg.blocks)
+        prof = capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+    exp, sum_u, _ = oracle.fps(pts, cfg.k, cfg.rng, cfg.blocks, stats=True)
+    assert prof.mode == MODE_GRID and prof.ctas_per_cloud == 64
+    assert np.array_equal(idx, exp)
+    assert prof.ref_points_updated == sum_u
+    assert prof.points_evaluated <= prof.ref_points_updated
