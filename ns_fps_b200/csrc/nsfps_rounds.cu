@@ -98,6 +98,12 @@ constexpr int kSpec = NSFPS_SPEC_STEPS;
 static_assert((kBatch & (kBatch - 1)) == 0, "kBatch is a power of two");
 static_assert(kReplay == 1 || kReplay == 2 || kReplay == 4, "1, 2 or 4 replay warps");
 static_assert(kWorkers >= 64, "at least two leaf-owning warps");
+// Slots of 32 leaves per CTA, at most (kMaxLeavesPerThread * kWorkers / 32).
+constexpr int kMaxSlots = 64;
+static_assert(kMaxLeavesPerThread * kWorkers / 32 <= kMaxSlots, "slot mask holds every slot");
+// Parts of at least this many leaves per worker thread publish each sample
+// with the mask of the slots its cube reaches (see the kernel).
+constexpr int kMaskMinM = 4;
 
 struct __align__(16) Cand {
   float x, y, z, d;
@@ -107,6 +113,14 @@ struct __align__(16) Cand {
 struct Sample {
   float4 q;  // x, y, z, distance
   uint4 c;   // cube x, y, z, sorted position
+};
+// A queued sample with the mask of the slots its cube reaches (bit j: slot
+// j), for parts of kMaskMinM or more leaves per worker thread.
+struct MaskedSample {
+  float4 q;
+  uint4 c;
+  uint32_t hit[2];
+  uint32_t pad[2];
 };
 
 // One CTA's published list: its T farthest points and its bound.  Copied as
@@ -130,6 +144,7 @@ struct RoundCtl {
   uint32_t mleaf[T + 1];                    // the CTA's T+1 best leaves
   unsigned long long xkey[2][kReplay][kSpec];  // per replay warp best keys, by parity
   uint32_t scan[33];
+  uint2 sbox[kMaxSlots];  // slot-mask parts: per slot, packed lowest and highest cell
   uint32_t timed_out;  // warp 0's list wait gave up (read by the other replay warps)
   uint32_t produced;  // samples of this round queued so far (release/acquire)
   uint32_t done;      // the round's last sample is queued
@@ -236,7 +251,9 @@ fps_rounds_cluster(const LoopArgs a) {
   float4 *s_hi = s_lo + a.max_leaves;  // (hi.xyz, cell)
   uint32_t *s_gst = reinterpret_cast<uint32_t *>(s_hi + a.max_leaves);  // global sorted start
   float *s_tab = reinterpret_cast<float *>(s_gst + ((a.max_leaves + 3u) & ~3u));
-  Sample *s_samp = reinterpret_cast<Sample *>(s_tab + ((a.max_tab + 3u) & ~3u));
+  constexpr bool kMask = M >= kMaskMinM;  // see the slot layout below
+  using SampleT = std::conditional_t<kMask, MaskedSample, Sample>;
+  SampleT *s_samp = reinterpret_cast<SampleT *>(s_tab + ((a.max_tab + 3u) & ~3u));
 
   const RangeDev &Rg = a.ranges[a.rid[cloud]];
   const uint32_t n0 = Rg.blocks[0] - 1, n1 = Rg.blocks[1] - 1, n2 = Rg.blocks[2] - 1;
@@ -315,25 +332,42 @@ fps_rounds_cluster(const LoopArgs a) {
     }
   }
 
-  // per owned leaf, in registers.  The replay warps own no leaf; worker warp
-  // w (kReplay..) owns the `span` consecutive local leaves from
-  // (w - kReplay) * span, a spatially compact run (the leaves are in Morton
-  // order), as slots of 32: leaf m * 32 + lane of the run is its lane's m-th.
+  // per owned leaf, in registers.  The replay warps own no leaf.  The local
+  // leaves (Morton order) form slots of 32 consecutive leaves.
+  //  * Parts of fewer than kMaskMinM leaves per worker thread: worker warp w
+  //    (kReplay..) owns the `span` consecutive local leaves from
+  //    (w - kReplay) * span, a spatially compact run; its lane's m-th leaf is
+  //    leaf m * 32 + lane of the run.  Each worker tests every sample's cube
+  //    against its run's cell box and its slots' boxes.
+  //  * Larger parts (kMask): slot j belongs to worker warp j % W as its
+  //    (j / W)-th, so a sample's cube (a few consecutive slots) spreads its
+  //    leaf updates over the worker warps, and the replay warps test the
+  //    cube against every slot's box once, publishing the mask of the slots
+  //    it reaches with the sample; a worker skips a sample that reaches none
+  //    of its slots after one load.  Measured on parts of 6 leaves per
+  //    thread (c4, c5) this trims the workers' backlog at each round's end;
+  //    on small parts the replay warps' extra test costs more than it saves.
   constexpr uint32_t kWorkerWarps = (uint32_t)kWorkers / 32u;
   const uint32_t span = (nl + kWorkerWarps - 1u) / kWorkerWarps;
   const int widx = worker_index(warp);
   const uint32_t wbase = widx >= 0 ? (uint32_t)widx * span : 0u;
+  auto lidx = [&](int m, uint32_t ln) {
+    return kMask ? ((uint32_t)m * kWorkerWarps + (uint32_t)(widx >= 0 ? widx : 0)) * 32u + ln
+                 : wbase + (uint32_t)m * 32u + ln;
+  };
   auto owned = [&](int m, uint32_t ln) {
+    if (kMask) return widx >= 0 && lidx(m, ln) < nl;
     const uint32_t r = (uint32_t)m * 32u + ln;
     return widx >= 0 && r < span && wbase + r < nl;
   };
+  const uint32_t nslots = (nl + 31u) / 32u;
   uint32_t cell[M], cnt[M], gst[M], gpos[M], sbox_lo[M], sbox_hi[M];
   uint32_t lsc[M];  // shared-memory start | count << 16
   float lmax[M], bx0[M], by0[M], bz0[M], bx1[M], by1[M], bz1[M];
   uint32_t wx0 = 1023u, wy0 = 1023u, wz0 = 1023u, wx1 = 0u, wy1 = 0u, wz1 = 0u;
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint32_t i = wbase + (uint32_t)m * 32u + (uint32_t)lane;
+    const uint32_t i = lidx(m, (uint32_t)lane);
     if (owned(m, lane)) {
       const uint32_t g = gleaf(i);
       const float4 lo = a.leaf_lo[g], hi = a.leaf_hi[g];
@@ -368,6 +402,10 @@ fps_rounds_cluster(const LoopArgs a) {
     y1 = __reduce_max_sync(kFull, y1); z1 = __reduce_max_sync(kFull, z1);
     sbox_lo[m] = pack_cell(x0, y0, z0);
     sbox_hi[m] = pack_cell(x1, y1, z1);
+    if (kMask && widx >= 0 && lane == 0) {
+      const uint32_t j = (uint32_t)m * kWorkerWarps + (uint32_t)widx;
+      if (j < nslots) ctl.sbox[j] = make_uint2(sbox_lo[m], sbox_hi[m]);
+    }
     wx0 = min(wx0, x0); wy0 = min(wy0, y0); wz0 = min(wz0, z0);
     wx1 = max(wx1, x1); wy1 = max(wy1, y1); wz1 = max(wz1, z1);
   }
@@ -382,6 +420,20 @@ fps_rounds_cluster(const LoopArgs a) {
   }
   __syncthreads();
   cluster_sync_all();  // every CTA's mbarriers are armed before any remote write
+
+  // kMask: every replay lane holds the cell boxes of slots lane and 32 + lane
+  // (unpacked: x0, x1, y0, y1, z0, z1), for the mask words 0 and 1
+  uint32_t rsb[2][6];
+  bool rs_ok[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t j = 32u * (uint32_t)h + (uint32_t)lane;
+    rs_ok[h] = kMask && warp < kReplay && j < nslots;
+    const uint2 bx = rs_ok[h] ? ctl.sbox[j] : make_uint2(0u, 0u);
+    rsb[h][0] = bx.x & 1023u; rsb[h][1] = bx.y & 1023u;
+    rsb[h][2] = (bx.x >> 10) & 1023u; rsb[h][3] = (bx.y >> 10) & 1023u;
+    rsb[h][4] = bx.x >> 20; rsb[h][5] = bx.y >> 20;
+  }
 
   uint32_t u_ref = 0, u_eval = 0;
   uint32_t it = 1;           // next sample index (sample 0 is point 0)
@@ -400,25 +452,42 @@ fps_rounds_cluster(const LoopArgs a) {
     float qx[kBatch], qy[kBatch], qz[kBatch];
     uint32_t c0[kBatch], c1[kBatch], c2[kBatch];
     uint32_t live = 0u;
+    // slots whose cell box the cubes reach (uniform over the warp)
+    uint32_t act[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) act[m] = 0u;
+    if constexpr (kMask) {
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const bool on = (uint32_t)j < nb;
+        const uint2 hw = on ? *reinterpret_cast<const uint2 *>(s_samp[s0 + j].hit) : make_uint2(0u, 0u);
+        const unsigned long long mine = (((unsigned long long)hw.y << 32) | hw.x) >> widx;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const uint32_t b = (uint32_t)(mine >> ((uint32_t)m * kWorkerWarps)) & 1u;
+          act[m] |= b << j;
+          live |= b << j;
+        }
+      }
+      if (live == 0u) return;
+    }
 #pragma unroll
     for (int j = 0; j < kBatch; ++j) {
-      const bool on = (uint32_t)j < nb;
+      const bool on = (uint32_t)j < nb && (!kMask || ((live >> j) & 1u) != 0u);
       const float4 q = on ? s_samp[s0 + j].q : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       const uint4 cb = on ? s_samp[s0 + j].c : make_uint4(kNoCell, kNoCell, kNoCell, 0u);
       qx[j] = q.x; qy[j] = q.y; qz[j] = q.z;
       c0[j] = cb.x; c1[j] = cb.y; c2[j] = cb.z;
-      live |= cube_misses(cb.x, cb.y, cb.z, wbox_lo, wbox_hi) ? 0u : (1u << j);
+      if (!kMask) live |= cube_misses(cb.x, cb.y, cb.z, wbox_lo, wbox_hi) ? 0u : (1u << j);
     }
-    if (live == 0u) return;
-    // slots whose cell box the cubes reach (uniform over the warp)
-    uint32_t act[M];
+    if (!kMask) {
+      if (live == 0u) return;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      act[m] = 0u;
+      for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j)
-        act[m] |= (((live >> j) & 1u) &&
-                   !cube_misses(c0[j], c1[j], c2[j], sbox_lo[m], sbox_hi[m])) ? (1u << j) : 0u;
+        for (int j = 0; j < kBatch; ++j)
+          act[m] |= (((live >> j) & 1u) &&
+                     !cube_misses(c0[j], c1[j], c2[j], sbox_lo[m], sbox_hi[m])) ? (1u << j) : 0u;
     }
     uint32_t needb[M];
 #pragma unroll
@@ -518,7 +587,7 @@ fps_rounds_cluster(const LoopArgs a) {
       for (int m = 0; m < M; ++m)
         if (rk[m] >= 0) {
           ctl.wkey[widx][rk[m]] = pkey(lmax[m], gpos[m]);
-          ctl.wleaf[widx][rk[m]] = wbase + (uint32_t)m * 32u + (uint32_t)lane;
+          ctl.wleaf[widx][rk[m]] = lidx(m, (uint32_t)lane);
         }
     } else if (warp == 0 && lane == 0) {
       ctl.produced = 0u;
@@ -905,10 +974,25 @@ fps_rounds_cluster(const LoopArgs a) {
 #pragma unroll
               for (int j = 0; j < kSpec; ++j)
                 if ((uint32_t)j < m) {
-                  Sample sm;
+                  SampleT sm;
                   sm.q = make_float4(wx[j], wy[j], wz[j], wd[j]);
                   sm.c = make_uint4(wcube[j][0], wcube[j][1], wcube[j][2],
                                     pbase + (((1u << (32 - kSlotBits)) - 1u) - ((uint32_t)wt[j] >> kSlotBits)));
+                  if constexpr (kMask) {  // the slots whose cell box the cube reaches
+                    uint32_t cl[3], ch[3];  // the cube's cell range (empty: lo 0xffff)
+#pragma unroll
+                    for (int d = 0; d < 3; ++d) {
+                      cl[d] = wcube[j][d] & 0xffffu;
+                      ch[d] = cl[d] + (wcube[j][d] >> 16);
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                      sm.hit[h] = __ballot_sync(
+                          kFull, rs_ok[h] && cl[0] <= rsb[h][1] && ch[0] >= rsb[h][0] &&
+                                     cl[1] <= rsb[h][3] && ch[1] >= rsb[h][2] &&
+                                     cl[2] <= rsb[h][5] && ch[2] >= rsb[h][4]);
+                    sm.pad[0] = sm.pad[1] = 0u;
+                  }
                   s_samp[n + j] = sm;
                 }
               st_release_cta_if(warp == 0 && lane == 0, &ctl.produced, n + m);  // workers may apply them
@@ -1101,7 +1185,7 @@ int rounds_leaves_per_thread(uint32_t leaves) {
 size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab) {
   return (size_t)pts * 16 + (size_t)leaves * 32 + (size_t)((leaves + 3) & ~3u) * 4 +
          (size_t)((tab + 3) & ~3u) * 4 +
-         (size_t)kQueue * sizeof(Sample);
+         (size_t)kQueue * sizeof(MaskedSample);
 }
 
 int rounds_max_smem(uint32_t P) {
