@@ -1,11 +1,14 @@
-"""GPU parity of the grid-wide round loop (one cloud of at least 98,304 points
-spread over 64 or 128 co-resident CTAs, 384 or 512 published candidates per
-round) on seeded random clouds, against the CPU oracle: bit-exact indices.
+"""GPU parity of the large-cloud layouts of the round loop against the CPU
+oracle: bit-exact indices.
 
-The golden vectors pin this path on the c2 and c4 configs only; these cases
-add exact distance ties (quantised coordinates), clamped outliers (ranges
-narrower than the data), clustered and flat clouds, and several direct
-(power-of-two) grids, and check that the grid-wide loop is what ran.
+* The grid-wide loop (one cloud of at least 98,304 points over 64 or 128
+  co-resident CTAs, 384 or 512 published candidates per round) on seeded
+  random clouds: the golden vectors pin it on the c2 and c4 configs only;
+  these cases add exact distance ties (quantised coordinates), clamped
+  outliers (ranges narrower than the data), clustered and flat clouds and
+  several direct (power-of-two) grids, and check that it is what ran.
+* A batch of LiDAR scans, one cluster per scan with ~6 leaves per worker
+  thread: slots dealt over the worker warps, samples queued with slot masks.
 """
 import numpy as np
 import pytest
@@ -73,3 +76,26 @@ def test_grid_loop_work_counter_equals_reference_work():
     assert np.array_equal(idx, exp)
     assert prof.ref_points_updated == sum_u
     assert prof.points_evaluated <= prof.ref_points_updated
+
+
+MODE_CLUSTER_ROUNDS = 2  # nsfps_profile.mode of the round loop in one cluster per cloud
+
+
+def test_batched_scans_large_parts_match_oracle():
+    """A batch of LiDAR scans (c5's generator) runs one cluster of 16 CTAs per
+    scan with about 6 leaves per worker thread: the layout whose slots are
+    dealt over the worker warps and whose samples carry a slot mask."""
+    from ns_fps_b200 import synthetic as S
+    cfg = S.CONFIGS["c5"]
+    clouds = S.make("c5", seed=300, count=3)
+    k = 4000
+    capi.set_profiling(True)
+    try:
+        got = capi.fps_batched(clouds, k, cfg.rng, cfg.blocks)
+        prof = capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+    assert prof.mode == MODE_CLUSTER_ROUNDS and prof.ctas_per_cloud == 16, (prof.mode, prof.ctas_per_cloud)
+    for i, cl in enumerate(clouds):
+        exp = oracle.fps(cl, k, cfg.rng, cfg.blocks)
+        assert np.array_equal(got[i], exp), f"scan {i}"
