@@ -25,14 +25,17 @@
 // sequence, so all agree on every sample and on when to stop.
 //
 // A round, per CTA:
-//   1. top-(T+1) points: each warp picks its T+1 best leaves by leaf maximum;
-//      warp 0 merges them to the CTA's T+1 best leaves (the T+1 best points
-//      lie in those leaves), gathers their points and selects the T+1 best;
-//   2. st.async the T candidates and the bound to every CTA; wait (mbarrier)
-//      for all P lists;
-//   3. warp 0 replays steps on the candidates, queueing each decided sample
-//      (point, distance, cube, position) in shared memory;
-//   4. at the same time the worker warps (1..7, which own all the leaves)
+//   1. top-(T+1) points: each worker warp picks its T+1 best leaves by leaf
+//      maximum; warp 0 merges them to the CTA's T+1 best leaves (the T+1
+//      best points lie in those leaves), gathers their points and selects
+//      the T+1 best;
+//   2. a bulk copy of the T candidates and the bound into every CTA of the
+//      cluster, then a wait (mbarrier) for all P lists; in the grid-wide
+//      variant, lists in global memory and an arrival counter;
+//   3. the two replay warps (0, 1) replay steps on the candidates, queueing
+//      each decided sample (point, distance, cube, position) in shared
+//      memory;
+//   4. at the same time the worker warps (2..7, which own all the leaves)
 //      apply the queued samples to their leaves, in order, as they appear
 //      (release/acquire on a shared counter).
 //
