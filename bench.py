@@ -24,6 +24,11 @@ runs the 256-scan batch split over the ranks instead (strong scaling).
   cpu_baseline  the reference's yuezu_fps() compiled from its own sources
           (oracle/_ref), timed on this host on a bounded sample.
 
+  batch_c5  every line also carries the 256-scan batch (config 5) split over
+          the ranks (strong scaling: 256 / N scans per rank): samples/s of the
+          whole box over the slowest rank's device time, each rank's time,
+          and the reference CPU on 16 threads (--no-batch-c5 skips it).
+
 `--impl reference` times the reference CPU implementation alone on the same
 workload with the host threads it can use (rank 0 only under torchrun).
 
@@ -49,6 +54,16 @@ from ns_fps_b200 import dist as D  # noqa: E402
 from ns_fps_b200 import synthetic as S  # noqa: E402
 
 METRIC = "FPS samples/sec (whole box) at 1/2/4/8 B200; ms per 122,880→16,384 scan"
+L2_NOTE = "GPU arm: 256 MiB L2 flush between steps, outside the timed window"
+# shared memory bytes per clock per SM (B200), for the sampling loop's SMEM figure
+SMEM_BYTES_PER_CLK = 128
+
+
+def config_dict(name: str):
+    """The workload as both arms describe it (identical dicts)."""
+    cfg = S.CONFIGS[name]
+    return {"workload": name, "points": cfg.n, "k": cfg.k, "blocks": list(cfg.blocks),
+            "range": list(cfg.rng), "clouds": cfg.clouds, "l2": L2_NOTE}
 
 
 def parse():
@@ -59,6 +74,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch-c5", action="store_true",
+                    help="skip the 256-scan batch sub-record")
+    ap.add_argument("--c5-steps", type=int, default=2, help="timed steps of the batch_c5 record")
     ap.add_argument("--path", choices=["fps", "group"], default="fps",
                     help="fps: the sampler (default); group: the ball query after it")
     ap.add_argument("--radius", type=float, default=0.5, help="--path group: ball radius")
@@ -221,8 +239,7 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "clouds_per_step": len(clouds), "points": cfg.n,
-                   "k": cfg.k, "blocks": list(cfg.blocks)},
+        "config": config_dict(args.workload), "clouds_per_step": len(clouds),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": kind,
                          "sample": f"{len(clouds)} whole cloud(s) per step, {threads} thread(s)"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
@@ -230,6 +247,67 @@ def run_reference(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def batch_c5(args, rank: int, world: int, dev, capi, flush, stream):
+    """The 256-scan batch (config 5) split over the ranks, strong scaling:
+    rank r samples scans r, r + N, ... as one nsfps_fps_device call per step,
+    timed with CUDA events (warm-up 1, args.c5_steps timed steps, the L2 flush
+    between steps).  Every rank takes the same collective steps.  Returns the
+    record on rank 0, None elsewhere."""
+    import torch
+    cfg, clouds, _, per = workload_clouds("c5", rank, world)
+    offsets = np.zeros(len(clouds) + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum([c.shape[0] for c in clouds])
+    d_xyz = torch.from_numpy(np.concatenate(clouds, axis=0)).to(dev)
+    d_out = torch.empty(len(clouds) * cfg.k, dtype=torch.int64, device=dev)
+
+    def step():
+        return capi.fps_device(d_xyz.data_ptr(), offsets, cfg.k, (cfg.rng, cfg.blocks), False,
+                               d_out.data_ptr(), stream.cuda_stream)
+
+    step()
+    torch.cuda.synchronize(dev)
+    D.barrier(dev.index)
+    samples, ms = 0, 0.0
+    for _ in range(max(1, args.c5_steps)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        samples += sum(step())
+        b.record(stream)
+        b.synchronize()
+        ms += a.elapsed_time(b)
+    steps = max(1, args.c5_steps)
+    mine = np.zeros(world)
+    mine[rank] = ms / steps
+    rank_ms = D.sum_over_ranks(list(mine), device=dev)
+    total = D.sum_over_ranks([samples], device=dev)[0]
+    del d_xyz, d_out
+    if rank != 0:
+        return None
+    slow, fast = max(rank_ms), min(rank_ms)
+    rec = {"workload": "c5", "value": total / steps / (slow / 1e3), "unit": "samples/s",
+           "scaling": "strong", "scans": cfg.clouds, "scans_per_gpu": per,
+           "ms_per_step": slow, "rank_ms": rank_ms, "slowest_over_fastest": slow / fast,
+           "steps": steps, "warmup": 1}
+    if not args.no_cpu_baseline:
+        import oracle
+        threads = min(16, os.cpu_count() or 1)
+        sample = clouds[:threads] if len(clouds) >= threads else \
+            [S.lidar_scan(i) for i in range(threads)]
+        if oracle.have_ref():
+            outs, secs = oracle.ref_fps_many(sample, cfg.k, cfg.rng, cfg.blocks, threads=threads)
+            kind = "reference"
+        else:
+            t0 = time.perf_counter()
+            outs = [oracle.fps(c, cfg.k, cfg.rng, cfg.blocks) for c in sample[:1]]
+            secs, kind, threads = time.perf_counter() - t0, "port", 1
+        rec["reference_cpu"] = {"value": sum(len(o) for o in outs) / secs, "unit": "samples/s",
+                                "cores": threads, "kind": kind,
+                                "sample": f"{len(outs)} whole scan(s) on {threads} thread(s), "
+                                          f"{secs:.2f} s"}
+    return rec
 
 
 def run_ours(args):
@@ -306,6 +384,11 @@ def run_ours(args):
             e2e_times.append(dt)
     e2e_s = float(np.mean(e2e_times))
 
+    # ---- the 256-scan batch over the ranks (all ranks, same collectives)
+    batch = None
+    if not args.no_batch_c5 and args.workload != "c5":
+        batch = batch_c5(args, rank, world, dev, capi, flush, stream)
+
     # ---- aggregate over ranks (max of times, sum of work)
     mx = D.max_over_ranks([my_ms, e2e_s], device=dev)
     sm = D.sum_over_ranks([samples, e2e_n, ref_pts, len(clouds)], device=dev)
@@ -323,14 +406,19 @@ def run_ours(args):
         peak, peak_kind = measured_peaks()
         traffic = profiled_traffic(args.workload)
         iters = samples / max(len(clouds), 1) / args.steps
+        clocks = clk.summary()
+        # the loop keeps the cloud in shared memory: its operative bound is the
+        # serial step chain (us_per_iteration); for scale, the same algorithmic
+        # bytes against the shared-memory bandwidth of the SMs it occupies
+        sm_used = min(148, int(prof.ctas_per_cloud) * len(clouds))
+        mhz = clocks.get("sm_mhz") or 1965.0
+        smem_peak = sm_used * SMEM_BYTES_PER_CLK * mhz * 1e6 / 1e9
         result = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "clouds_per_gpu": len(clouds), "points": cfg.n,
-                       "k": k, "blocks": list(cfg.blocks), "range": list(cfg.rng),
-                       "l2": "256 MiB flush between steps, outside the timed window"},
+            "config": config_dict(args.workload), "clouds_per_gpu": len(clouds),
             "ms_per_scan": my_ms / args.steps / max(len(clouds), 1) if per == 1 else None,
             "us_per_iteration": (loop_ms / args.steps) * 1e3 / max(iters, 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -339,13 +427,21 @@ def run_ours(args):
                          "kernel": "fps_rounds_cluster" if loop_mode in (2, 3) else "fps_loop_cluster",
                          "algorithmic_bytes_per_launch": alg_bytes / args.steps,
                          "kernel_ms_per_launch": loop_ms / args.steps,
-                         "points_evaluated_per_launch": evals / args.steps},
+                         "points_evaluated_per_launch": evals / args.steps,
+                         "operative_bound": "latency: the serial step chain (us_per_iteration); "
+                                            "the cloud is shared-memory resident",
+                         "smem": {"achieved": achieved, "peak": smem_peak, "unit": "GB/s",
+                                  "frac": achieved / smem_peak, "sms": sm_used,
+                                  "peak_basis": f"{SMEM_BYTES_PER_CLK} B/clk/SM x {sm_used} SMs "
+                                                f"x {mhz:.0f} MHz"}},
             "e2e": {"value": e2e_value, "unit": "samples/s",
                     "h2d_bytes_per_step": int(12 * n_pts),
                     "d2h_bytes_per_step": int(8 * k * len(clouds) + 8 * len(clouds))},
             "gpu_launches": int(launches),
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
+        if batch is not None:
+            result["batch_c5"] = batch
         if not args.no_cpu_baseline:
             cfgc = S.CONFIGS[args.workload]
             threads = 1 if per == 1 else min(len(clouds), os.cpu_count() or 1)

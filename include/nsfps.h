@@ -159,6 +159,17 @@ NSFPS_API int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets,
                      int per_cloud_ranges, uint64_t *d_out, uint64_t *out_len,
                      void *stream);
 
+/* fps_with_bbox() for device-resident clouds: nsfps_fps_device with every
+ * cloud's bounding box (reduced on the device, widened by BOUNDARY_EPS as in
+ * compute_bbox) and x_blocks x y_blocks x z_blocks blocks (replaces the
+ * binding yuezu_fps/yuezu_fps_pybind.cpp:88-101 and src/yuezu_fps.cpp:
+ * 643-670 for clouds in HBM; it is also the range the reference's KITTI
+ * benchmark builds, eval/src_cpu/compare_cpu_test_kitti.cpp:230-245). */
+NSFPS_API int nsfps_fps_device_with_bbox(const float *d_xyz, const uint64_t *offsets,
+                               uint64_t count, uint64_t k, uint32_t x_blocks,
+                               uint32_t y_blocks, uint32_t z_blocks, uint64_t *d_out,
+                               uint64_t *out_len, void *stream);
+
 /* Limits of nsfps_fps_device_static(): points per call, and the size of the
  * fixed device scratch array that holds every intermediate buffer. */
 #define NSFPS_STATIC_MAX_POINTS 65536u
@@ -270,6 +281,35 @@ typedef struct nsfps_profile {
 
 NSFPS_API int nsfps_set_profiling(int enable);
 NSFPS_API int nsfps_last_profile(nsfps_profile *out);
+
+/* ---- Test hooks.  No counterpart in the reference, whose GPU prototype
+ * ignores CUDA errors (eval/src_gpu/yuezu_fps_gpu_optimized.cu:904-910) and
+ * whose CPU path has no failure mode to test.  They drive this engine's error
+ * paths without faulting the GPU:
+ *   wait_limit_ns      limit of every bounded in-kernel wait (0 = the default,
+ *                      2 s; the queue polling of worker warps gets twice it)
+ *   withhold_cta       rank, among the CTAs of cloud 0, of one CTA that does
+ *                      not publish its round-`withhold_step` candidate list
+ *                      (round loops) or its step-`withhold_step` proposals
+ *                      (per-step loop); every wait for it then runs out and
+ *                      the call returns NSFPS_ERR_TIMEOUT with the device
+ *                      still usable.  -1 = none.
+ *   withhold_step      the round (round loops, from 0) or step (per-step loop,
+ *                      from 1) at which it withholds
+ *   fail_alloc_device  the next workspace request of an allocating entry point
+ *                      on this device fails as if cudaMalloc had run out of
+ *                      memory (NSFPS_ERR_OOM); it fires once.  -1 = none.
+ * The hooks are process-wide and stay set until replaced; NULL restores the
+ * defaults.  Not for production use. */
+typedef struct nsfps_test_hooks {
+  uint64_t wait_limit_ns;
+  int32_t withhold_cta;
+  uint32_t withhold_step;
+  int32_t fail_alloc_device;
+  int32_t reserved;
+} nsfps_test_hooks;
+
+NSFPS_API int nsfps_set_test_hooks(const nsfps_test_hooks *hooks);
 
 #ifdef __cplusplus
 }

@@ -65,11 +65,23 @@ def rng(bounds, blocks) -> Range:
 
 
 def fps(points, k, bounds=None, blocks=(16, 16, 16), device=0):
-    """nsfps_fps; bounds None = compute_bbox(16^3) like fps(range=None)."""
+    """nsfps_fps.  bounds None: the cloud's bounding box (compute_bbox) with
+    `blocks` -- nsfps_fps with a NULL range for 16^3 (fps(range=None)),
+    nsfps_fps_with_bbox otherwise (fps_with_bbox)."""
     p = np.ascontiguousarray(np.asarray(points, dtype=np.float32))
     n = p.shape[0]
     out = np.zeros(max(min(int(k), n), 1), dtype=np.uint64)
     ln = ctypes.c_uint64(0)
+    if bounds is None and tuple(int(b) for b in blocks) != (16, 16, 16):
+        xb, yb, zb = (int(b) for b in blocks)
+        rc = lib().nsfps_fps_with_bbox(p.ctypes.data_as(_f32p), ctypes.c_uint64(n),
+                                       ctypes.c_uint64(int(k)), ctypes.c_uint32(xb),
+                                       ctypes.c_uint32(yb), ctypes.c_uint32(zb),
+                                       out.ctypes.data_as(_u64p), ctypes.byref(ln),
+                                       ctypes.c_int(device))
+        if rc != OK:
+            raise RuntimeError(f"nsfps_fps_with_bbox rc={rc}: {last_error()}")
+        return out[:ln.value].copy()
     r = rng(bounds, blocks) if bounds is not None else None
     rc = lib().nsfps_fps(p.ctypes.data_as(_f32p), ctypes.c_uint64(n), ctypes.c_uint64(int(k)),
                          ctypes.byref(r) if r is not None else None,
@@ -98,6 +110,24 @@ def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
     if rc != OK:
         raise RuntimeError(f"nsfps_fps_batched rc={rc}: {last_error()}")
     return [o[:lens[i]].copy() for i, o in enumerate(outs)]
+
+
+class TestHooks(ctypes.Structure):
+    _fields_ = [("wait_limit_ns", ctypes.c_uint64), ("withhold_cta", ctypes.c_int32),
+                ("withhold_step", ctypes.c_uint32), ("fail_alloc_device", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
+def set_test_hooks(wait_limit_ns: int = 0, withhold_cta: int = -1, withhold_step: int = 0,
+                   fail_alloc_device: int = -1, reset: bool = False):
+    """nsfps_set_test_hooks (test use only): the in-kernel wait limit, one CTA
+    that withholds its list / proposals at one round / step, a one-shot
+    failed workspace request.  reset=True restores the defaults."""
+    h = None if reset else TestHooks(int(wait_limit_ns), int(withhold_cta), int(withhold_step),
+                                      int(fail_alloc_device), 0)
+    rc = lib().nsfps_set_test_hooks(ctypes.byref(h) if h is not None else None)
+    if rc != OK:
+        raise RuntimeError(f"nsfps_set_test_hooks rc={rc}: {last_error()}")
 
 
 def set_profiling(on: bool):
@@ -138,6 +168,25 @@ def fps_device(d_xyz_ptr: int, offsets, k: int, ranges, per_cloud: bool, d_out_p
                                 ctypes.c_void_p(d_out_ptr), lens, ctypes.c_void_p(stream_ptr))
     if rc != OK:
         raise RuntimeError(f"nsfps_fps_device rc={rc}: {last_error()}")
+    return [int(v) for v in lens]
+
+
+def fps_device_with_bbox(d_xyz_ptr: int, offsets, k: int, blocks, d_out_ptr: int,
+                         stream_ptr: int = 0):
+    """nsfps_fps_device_with_bbox: as fps_device with each cloud's bounding
+    box (reduced on the device) and `blocks` blocks.  Returns the per-cloud
+    sample counts."""
+    count = len(offsets) - 1
+    offs = (ctypes.c_uint64 * (count + 1))(*[int(o) for o in offsets])
+    lens = (ctypes.c_uint64 * count)()
+    xb, yb, zb = (int(b) for b in blocks)
+    rc = lib().nsfps_fps_device_with_bbox(ctypes.c_void_p(d_xyz_ptr), offs, ctypes.c_uint64(count),
+                                          ctypes.c_uint64(int(k)), ctypes.c_uint32(xb),
+                                          ctypes.c_uint32(yb), ctypes.c_uint32(zb),
+                                          ctypes.c_void_p(d_out_ptr), lens,
+                                          ctypes.c_void_p(stream_ptr))
+    if rc != OK:
+        raise RuntimeError(f"nsfps_fps_device_with_bbox rc={rc}: {last_error()}")
     return [int(v) for v in lens]
 
 

@@ -37,6 +37,13 @@ std::atomic<int> g_profiling{0};
 // NSFPS_STEP_LOOP=1 in the environment selects the per-step loop even for
 // direct ranges (both loops return identical samples).
 std::atomic<int> g_force_steps{-1};
+// nsfps_set_test_hooks: wait limit, withheld list / proposal, failed
+// workspace request
+constexpr long long kDefaultWaitNs = 2000000000ll;
+std::atomic<long long> g_wait_ns{kDefaultWaitNs};
+std::atomic<int> g_hold_cta{-1};
+std::atomic<uint32_t> g_hold_step{0};
+std::atomic<int> g_fail_alloc{-1};
 }  // namespace
 
 int set_error(int code, const char *fmt, ...) {
@@ -203,6 +210,7 @@ struct DeviceCtx {
   size_t ws_bytes = 0;
   cudaEvent_t ev[4] = {};
   bool ready = false;
+  bool fixed = false;  // the workspace is the static scratch array: never (re)allocated
 };
 
 constexpr int kMaxDevices = 64;
@@ -332,7 +340,17 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
 }
 
 int ensure_ws(DeviceCtx *ctx, size_t bytes) {
+  if (!ctx->fixed) {
+    int want = ctx->device;
+    if (g_fail_alloc.load() == want && g_fail_alloc.compare_exchange_strong(want, -1))
+      return set_error(NSFPS_ERR_OOM,
+                       "workspace allocation on device %d failed (injected by "
+                       "nsfps_set_test_hooks)", ctx->device);
+  }
   if (ctx->ws_bytes >= bytes) return NSFPS_OK;
+  if (ctx->fixed)
+    return set_error(NSFPS_ERR_UNSUPPORTED, "needs %zu bytes of scratch, the fixed array holds %zu",
+                     bytes, ctx->ws_bytes);
   if (ctx->ws) {
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->ws);
@@ -574,7 +592,9 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   la.stats = b.stats;
   la.glist = b.glist;
   la.gbar = b.gbar;
-  la.timeout_ns = 2000000000ll;
+  la.timeout_ns = g_wait_ns.load();
+  la.hold_cta = g_hold_cta.load();
+  la.hold_step = g_hold_step.load();
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[2], st));
   NSFPS_CUDA(plan.rounds ? run_rounds(la, plan, st, launches) : run_loop(la, plan, st, launches));
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[3], st));
@@ -647,11 +667,12 @@ nsfps_range bbox_of(const float *xyz, uint64_t n, uint32_t xb, uint32_t yb, uint
   return r;
 }
 
-// compute_bbox(cloud, 16, 16, 16) of `count` device-resident clouds (the
-// reference's fps(range=None) path, src/yuezu_fps.cpp:643-670), with the
-// reduction on the device and the same float arithmetic as bbox_of after it.
+// compute_bbox(cloud, xb, yb, zb) of `count` device-resident clouds (the
+// reference's fps(range=None) and fps_with_bbox paths, src/yuezu_fps.cpp:
+// 643-670), with the reduction on the device and the same float arithmetic
+// as bbox_of after it.
 int device_bboxes(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz, const uint64_t *offsets,
-                  uint64_t count, std::vector<nsfps_range> &rs) {
+                  uint64_t count, const uint32_t blocks[3], std::vector<nsfps_range> &rs) {
   const size_t off_bytes = align_up(sizeof(uint32_t) * (count + 1), 256);
   int rc = ensure_ws(ctx, off_bytes + sizeof(float) * 6 * count);
   if (rc) return rc;
@@ -681,9 +702,9 @@ int device_bboxes(DeviceCtx *ctx, cudaStream_t st, const float *d_xyz, const uin
     r.min_x = b[0] - eps; r.max_x = b[3] + eps;
     r.min_y = b[1] - eps; r.max_y = b[4] + eps;
     r.min_z = b[2] - eps; r.max_z = b[5] + eps;
-    r.x_blocks = NSFPS_DEFAULT_X_BLOCKS;
-    r.y_blocks = NSFPS_DEFAULT_Y_BLOCKS;
-    r.z_blocks = NSFPS_DEFAULT_Z_BLOCKS;
+    r.x_blocks = blocks[0];
+    r.y_blocks = blocks[1];
+    r.z_blocks = blocks[2];
   }
   return NSFPS_OK;
 }
@@ -918,6 +939,7 @@ int get_static_ctx(int device, DeviceCtx **out) {
     c->ws = p;
     c->ws_bytes = bytes;
     c->device = device;
+    c->fixed = true;
     c->ready = true;
   }
   *out = c;
@@ -1092,10 +1114,15 @@ int nsfps_fps_with_bbox(const float *xyz, uint64_t n, uint64_t k, uint32_t x_blo
   return nsfps_fps(xyz, n, k, &r, out, out_len, device);
 }
 
-int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count,
-                     uint64_t k, const nsfps_range *ranges, int per_cloud_ranges,
-                     uint64_t *d_out, uint64_t *out_len, void *stream) {
-  clear_error();
+}  // extern "C"
+
+namespace nsfps {
+namespace {
+// nsfps_fps_device / nsfps_fps_device_with_bbox: ranges == NULL selects each
+// cloud's bounding box with bbox_blocks, reduced on the device.
+int fps_device_impl(const float *d_xyz, const uint64_t *offsets, uint64_t count, uint64_t k,
+                    const nsfps_range *ranges, int per_cloud_ranges, const uint32_t bbox_blocks[3],
+                    uint64_t *d_out, uint64_t *out_len, void *stream) {
   if (count == 0) return NSFPS_OK;
   if (!offsets || !out_len || !d_out || !d_xyz)
     return set_error(NSFPS_ERR_ARG, "NULL argument");
@@ -1121,7 +1148,7 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
   std::vector<nsfps_range> rs;
   std::vector<uint32_t> rid(count, 0);
   if (!ranges) {
-    rc = device_bboxes(ctx, user, d_xyz, offsets, count, rs);
+    rc = device_bboxes(ctx, user, d_xyz, offsets, count, bbox_blocks, rs);
     if (rc) return rc;
     for (uint64_t i = 0; i < count; ++i) rid[i] = (uint32_t)i;
   } else if (per_cloud_ranges) {
@@ -1139,6 +1166,29 @@ int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count
   if (rc) return rc;
   for (uint64_t i = 0; i < count; ++i) out_len[i] = lens[i];
   return NSFPS_OK;
+}
+}  // namespace
+}  // namespace nsfps
+
+extern "C" {
+
+int nsfps_fps_device(const float *d_xyz, const uint64_t *offsets, uint64_t count,
+                     uint64_t k, const nsfps_range *ranges, int per_cloud_ranges,
+                     uint64_t *d_out, uint64_t *out_len, void *stream) {
+  clear_error();
+  const uint32_t blocks[3] = {NSFPS_DEFAULT_X_BLOCKS, NSFPS_DEFAULT_Y_BLOCKS,
+                              NSFPS_DEFAULT_Z_BLOCKS};
+  return fps_device_impl(d_xyz, offsets, count, k, ranges, per_cloud_ranges, blocks, d_out,
+                         out_len, stream);
+}
+
+int nsfps_fps_device_with_bbox(const float *d_xyz, const uint64_t *offsets, uint64_t count,
+                               uint64_t k, uint32_t x_blocks, uint32_t y_blocks,
+                               uint32_t z_blocks, uint64_t *d_out, uint64_t *out_len,
+                               void *stream) {
+  clear_error();
+  const uint32_t blocks[3] = {x_blocks, y_blocks, z_blocks};
+  return fps_device_impl(d_xyz, offsets, count, k, nullptr, 0, blocks, d_out, out_len, stream);
 }
 
 int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k,
@@ -1177,7 +1227,12 @@ int nsfps_fps_device_static(const float *d_xyz, uint64_t n, uint64_t k,
   // the workspace already holds `need` bytes, so run_job allocates nothing
   std::vector<uint32_t> lens;
   rc = run_job(ctx, (cudaStream_t)stream, j, nullptr, nullptr, d_xyz, d_out, lens, nullptr);
-  if (rc) return rc;
+  if (rc) {
+    // an error may leave work queued on `stream` that still uses the array:
+    // drain it before the lock lets the next call in
+    cudaStreamSynchronize((cudaStream_t)stream);
+    return rc;
+  }
   *out_len = lens[0];
   return NSFPS_OK;
 }
@@ -1305,6 +1360,24 @@ int nsfps_group_points_device(const float *d_xyz, const uint64_t *point_offsets,
   if (d_centers) d_centers += 3 * center_offsets[0];
   return gather_on(ctx, (cudaStream_t)stream, d_xyz, poff, d_centers, coff, nsample, d_idx,
                    d_out);
+}
+
+int nsfps_set_test_hooks(const nsfps_test_hooks *h) {
+  clear_error();
+  if (!h) {
+    g_wait_ns.store(kDefaultWaitNs);
+    g_hold_cta.store(-1);
+    g_hold_step.store(0);
+    g_fail_alloc.store(-1);
+    return NSFPS_OK;
+  }
+  if (h->wait_limit_ns > (uint64_t)kDefaultWaitNs * 30)
+    return set_error(NSFPS_ERR_ARG, "wait_limit_ns above 60 s");
+  g_wait_ns.store(h->wait_limit_ns ? (long long)h->wait_limit_ns : kDefaultWaitNs);
+  g_hold_cta.store(h->withhold_cta < 0 ? -1 : h->withhold_cta);
+  g_hold_step.store(h->withhold_step);
+  g_fail_alloc.store(h->fail_alloc_device < 0 ? -1 : h->fail_alloc_device);
+  return NSFPS_OK;
 }
 
 int nsfps_set_profiling(int enable) {

@@ -105,7 +105,11 @@ struct LoopArgs {
   unsigned long long *stats;  // [0] reference-updated points, [1] evaluated
   uint4 *glist;               // grid-wide rounds: 2 * P published lists (global)
   uint32_t *gbar;             // grid-wide rounds: arrival counter (starts at 0)
-  long long timeout_ns;
+  long long timeout_ns;       // limit of every bounded wait
+  // test hook: CTA `hold_cta` of cloud 0 does not publish at round / step
+  // `hold_step` (-1: never), so that the waits for it run out
+  int32_t hold_cta;
+  uint32_t hold_step;
 };
 
 // Which shared-memory-resident sampling kernel to run.

@@ -292,7 +292,9 @@ fps_loop_cluster(const LoopArgs a) {
       }
       dirty = false;
     }
-    if ((uint32_t)lane < P) {
+    // test hook: one CTA of cloud 0 withholds its agents' proposals of a step
+    const bool hold = cloud == 0u && (int)crank == a.hold_cta && step == a.hold_step;
+    if ((uint32_t)lane < P && !hold) {
       const uint32_t b = step & (kBufs - 1);
       const uint32_t rs = r_slot0 + b * (uint32_t)sizeof(ctl.slot[0]);
       const uint32_t rk = r_key0 + b * (uint32_t)sizeof(ctl.key[0]);
@@ -451,10 +453,15 @@ fps_loop_cluster(const LoopArgs a) {
       atomicAdd(&a.stats[1], e64);
     }
   }
-  // Every remote write into this CTA's shared memory belongs to a step that
-  // every warp here has already waited for (all agents stop at the same step
-  // and nobody writes past it), so the CTA may exit without a final cluster
-  // barrier.
+  // ---- exit.  Normally every remote write into this CTA's shared memory
+  // belongs to a step every warp here has waited for (all agents stop at the
+  // same step and nobody writes past it).  After a wait ran out that no
+  // longer holds: a late agent may still write its proposals here.  So no
+  // CTA leaves before every CTA of the cluster is done writing: a cluster
+  // barrier, which every CTA reaches because every wait above is bounded.
+  // An agent writes a step's proposals before waiting (bounded) for that
+  // step, so they have landed by the time the last CTA arrives.
+  cluster_sync_all();
 }
 
 __global__ void epilogue_kernel(const uint32_t *__restrict__ out_rank,

@@ -703,10 +703,12 @@ fps_rounds_cluster(const LoopArgs a) {
           ctl.stage.bound = bound;
           ctl.stage.pad = 0ull;
         }
+        // test hook: one CTA of cloud 0 keeps this round's list to itself
+        const bool hold = cloud == 0u && (int)crank == a.hold_cta && round == a.hold_step;
         if (!GRID) {
           fence_proxy_async_smem();
           __syncwarp();
-          if ((uint32_t)lane < P) {
+          if ((uint32_t)lane < P && !hold) {
             const uint32_t ra = mapa(smem_u32(&ctl.list[buf][crank]), lane);
             const uint32_t rm = mapa(smem_u32(&ctl.mbar[buf]), lane);
             bulk_copy_to_cluster(ra, smem_u32(&ctl.stage), (uint32_t)sizeof(CtaList<T>), rm);
@@ -727,7 +729,10 @@ fps_rounds_cluster(const LoopArgs a) {
               if (__shfl_sync(kFull, now > deadline ? 1 : 0, 0)) { timed_out = true; break; }
             }
           }
-          if (lane == 0) mbar_arm(mb, tx_bytes);  // for round + kListBufs
+          // re-arm for round + kListBufs, only once this phase completed: a
+          // phase that never completed has no arrival left to take, and an
+          // arrive there is undefined
+          if (lane == 0 && !timed_out) mbar_arm(mb, tx_bytes);
         } else {
           // ---- publish to global memory, then a grid barrier (bounded).  Slot
           // (round & 1) is rewritten two rounds later, after every CTA passed
@@ -736,11 +741,12 @@ fps_rounds_cluster(const LoopArgs a) {
           constexpr int kWords = (int)(sizeof(CtaList<T>) / 16);
           const uint4 *src = reinterpret_cast<const uint4 *>(&ctl.stage);
           uint4 *dst = a.glist + ((size_t)(round & 1u) * P + crank) * kWords;
-          for (int w = lane; w < kWords; w += 32) __stcg(dst + w, src[w]);
+          if (!hold)
+            for (int w = lane; w < kWords; w += 32) __stcg(dst + w, src[w]);
           __syncwarp();  // lane 0's release below covers every lane's stores
           if (lane == 0) {
             const uint32_t target = (round + 1u) * P;
-            red_release_gpu_add(a.gbar, 1u);
+            if (!hold) red_release_gpu_add(a.gbar, 1u);
             unsigned long long deadline = 0;
             uint32_t polls = 0;
             while (ld_acquire_gpu(a.gbar) < target) {
@@ -1118,8 +1124,19 @@ fps_rounds_cluster(const LoopArgs a) {
       atomicAdd(&a.stats[1], e64);
     }
   }
-  // All CTAs replay the same steps, so they end in the same round; every
-  // remote write of that round was awaited, so no final cluster barrier.
+  // ---- exit.  Normally every CTA ends in the same round, and every remote
+  // write of that round was awaited.  After a wait ran out that no longer
+  // holds: a late CTA may still copy its list into this one.  So no CTA of a
+  // cluster leaves while another may still write its shared memory: warp 0's
+  // copies have read their source, then a cluster barrier, which every CTA
+  // reaches because every wait above is bounded.  A CTA issues each copy
+  // before at least one complete list wait or replay of its own, so the
+  // copies have landed by the time the last CTA arrives.
+  if (!GRID) {
+    if (warp == 0 && (uint32_t)lane < P) bulk_wait_read_all();
+    __syncwarp();
+    cluster_sync_all();
+  }
 }
 
 template <int M, int T, bool GRID, int CAP>

@@ -11,7 +11,18 @@ from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["load_bin"]
+__all__ = ["load_bin", "filter_records"]
+
+
+def filter_records(rec: np.ndarray, z_min: float = -5.0, return_index: bool = False):
+    """The benchmark's filter on (N, stride) records: the x, y, z of the
+    records with ``z >= z_min``, in file order (a NaN z is dropped, as
+    ``z >= -5`` is false), and optionally their record numbers."""
+    keep = rec[:, 2] >= np.float32(z_min)
+    pts = np.ascontiguousarray(rec[keep, :3], dtype=np.float32)
+    if return_index:
+        return pts, np.nonzero(keep)[0]
+    return pts
 
 
 def load_bin(path, stride: int = 4, z_min: float = -5.0, return_index: bool = False,
@@ -29,11 +40,10 @@ def load_bin(path, stride: int = 4, z_min: float = -5.0, return_index: bool = Fa
         raise ValueError(f"empty point cloud file: {path}")
     n = raw.size // stride
     rec = raw[: n * stride].reshape(n, stride)
-    keep = rec[:, 2] >= np.float32(z_min)  # NaN z is dropped, as `z >= -5` is false
-    pts = np.ascontiguousarray(rec[keep, :3], dtype=np.float32)
+    pts, idx = filter_records(rec, z_min, return_index=True)
     if device is not None:
         import torch
         pts = torch.from_numpy(pts).to(device)
     if return_index:
-        return pts, np.nonzero(keep)[0]
+        return pts, idx
     return pts

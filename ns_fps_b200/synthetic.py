@@ -105,6 +105,28 @@ def lidar_scan(seed: int = 0, beams: int = 64, steps: int = 1920,
     return np.ascontiguousarray(pts.astype(np.float32))
 
 
+def kitti_records(seed: int = 0, beams: int = 64, steps: int = 1948,
+                  below: int = 24) -> np.ndarray:
+    """A synthetic stand-in for one SemanticKITTI velodyne frame, as the
+    file's records: (N, 4) float32 x, y, z, remission.
+
+    The points are a ``lidar_scan`` of ``beams`` x ``steps`` rays (124,672 by
+    default, about a real frame's 124.7k); ``below`` random records are moved
+    below z = -5 m (the reference benchmark drops those,
+    eval/src_cpu/compare_cpu_test_kitti.cpp:202-216) and one record sits at
+    exactly z = -5 m (kept).  Remission is uniform on 0.00 .. 0.99 in steps of
+    0.01.  No dataset record is reproduced.
+    """
+    r = np.random.default_rng(10_000 + seed)
+    pts = lidar_scan(seed, beams=beams, steps=steps)
+    n = pts.shape[0]
+    idx = r.choice(n, below + 1, replace=False)
+    pts[idx[:below], 2] = r.uniform(-12.0, -5.001, below).astype(np.float32)
+    pts[idx[below], 2] = np.float32(-5.0)
+    rem = (r.integers(0, 100, n) / 100.0).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([pts, rem[:, None]], axis=1), dtype=np.float32)
+
+
 def sphere_cube_cloud(n: int = 16_384, seed: int = 0, sphere_fraction: float = 0.2,
                       n_spheres: int = 3) -> np.ndarray:
     """c3: uniform in [0,1]^3 with ``sphere_fraction`` of the points resampled

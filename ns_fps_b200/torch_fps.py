@@ -10,7 +10,7 @@ import builtins
 
 from . import capi
 
-__all__ = ["fps"]
+__all__ = ["fps", "fps_with_bbox"]
 
 
 def _range_arg(rng):
@@ -21,6 +21,39 @@ def _range_arg(rng):
                 (rng.x_blocks, rng.y_blocks, rng.z_blocks))
     bounds, blocks = rng
     return tuple(bounds), tuple(blocks)
+
+
+def _as_batch(points):
+    import torch
+    if not isinstance(points, torch.Tensor) or not points.is_cuda:
+        raise TypeError("points must be a CUDA tensor")
+    if points.dtype != torch.float32:
+        raise TypeError("points must be float32")
+    single = points.dim() == 2
+    if single:
+        points = points.unsqueeze(0)
+    if points.dim() != 3 or points.shape[2] != 3:
+        raise ValueError("Expected tensor with shape (N, 3) or (B, N, 3)")
+    return points.contiguous(), single
+
+
+def fps_with_bbox(points, sample_count: int, x_blocks: int = 16, y_blocks: int = 16,
+                  z_blocks: int = 16):
+    """``fps_with_bbox`` of CUDA tensors: each cloud's bounding box (reduced
+    on the device, widened by 1e-6 like compute_bbox) with the given block
+    counts.  Shapes and results as in ``fps``."""
+    import torch
+    pts, single = _as_batch(points)
+    B, N = int(pts.shape[0]), int(pts.shape[1])
+    k = int(sample_count)
+    out = torch.empty(B * k, dtype=torch.int64, device=pts.device)
+    with torch.cuda.device(pts.device):
+        stream = torch.cuda.current_stream(pts.device)
+        lens = capi.fps_device_with_bbox(pts.data_ptr(), [i * N for i in builtins.range(B + 1)],
+                                         k, (x_blocks, y_blocks, z_blocks), out.data_ptr(),
+                                         stream.cuda_stream)
+    res = [out[i * k: i * k + lens[i]] for i in builtins.range(B)]
+    return res[0] if single else res
 
 
 def fps(points, sample_count: int, range=None):
@@ -38,16 +71,7 @@ def fps(points, sample_count: int, range=None):
     stops early (every remaining point at distance 0).
     """
     import torch
-    if not isinstance(points, torch.Tensor) or not points.is_cuda:
-        raise TypeError("points must be a CUDA tensor")
-    if points.dtype != torch.float32:
-        raise TypeError("points must be float32")
-    single = points.dim() == 2
-    if single:
-        points = points.unsqueeze(0)
-    if points.dim() != 3 or points.shape[2] != 3:
-        raise ValueError("Expected tensor with shape (N, 3) or (B, N, 3)")
-    pts = points.contiguous()
+    pts, single = _as_batch(points)
     B, N = int(pts.shape[0]), int(pts.shape[1])
     k = int(sample_count)
     out = torch.empty(B * k, dtype=torch.int64, device=pts.device)

@@ -29,3 +29,18 @@ def yf():
 def capi():
     from tests import capi as c
     return c
+
+
+def reference_dir():
+    """The reference checkout when this machine has one (never the GPU box):
+    $NSFPS_REFERENCE_DIR, else BASELINE.json's reference_path; None when
+    absent."""
+    import json
+    ref = os.environ.get("NSFPS_REFERENCE_DIR")
+    if not ref:
+        try:
+            with open(os.path.join(ROOT, "BASELINE.json")) as f:
+                ref = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            ref = None
+    return ref if ref and os.path.isdir(ref) else None

@@ -13,6 +13,11 @@ Families:
                clip the data)
   * edge_*     duplicates, exact ties, clamped outliers, non-power-of-two
                grids (bucket collisions), tiny clouds, degenerate ranges
+  * kitti_*    the reference KITTI benchmark's setting
+               (eval/src_cpu/compare_cpu_test_kitti.cpp:202-245): records
+               filtered to z >= -5, the bounding box +- 1e-6 with 128 x 128 x 2
+               blocks, on synthetic frames (ns_fps_b200.synthetic.kitti_records)
+  * wide_*     power-of-two grids with more than 64 blocks on an axis
 """
 from __future__ import annotations
 
@@ -158,6 +163,33 @@ def _edge() -> List[Case]:
     return cases
 
 
+def _kitti_like(seed: int, every: int = 1):
+    from ns_fps_b200 import kitti
+
+    def f():
+        return kitti.filter_records(S.kitti_records(seed)[::every])
+    return f
+
+
+def _wide() -> List[Case]:
+    out = [
+        # a whole frame: one cloud of >= 98,304 points (the grid-wide loop)
+        Case("kitti_like_f0_128x128x2", _kitti_like(0), 16384, None, (128, 128, 2)),
+        # every 6th record: ~20.8k points (the round loop in one cluster)
+        Case("kitti_like_f1_sub6_128x128x2", _kitti_like(1, 6), 4096, None, (128, 128, 2)),
+    ]
+    # (the reference's cube list reserve() takes (2nx+1)(2ny+1)(2nz+1) entries
+    # in int, src/yuezu_fps.cpp:574, so the other axes' blocks stay wide)
+    r = np.random.RandomState(77)
+    w = (r.rand(20000, 3) * 1000.0).astype(np.float32)
+    out.append(Case("wide_1024x2x2", lambda w=w: w, 3000, (0, 1000, 0, 1000, 0, 1000),
+                    (1024, 2, 2), store_points=True))
+    out.append(Case("wide_2x256x4_100k", lambda: (np.random.RandomState(78).rand(100_000, 3)
+                                                   * 1000.0).astype(np.float32),
+                    3000, (0, 1000, 0, 1000, 0, 1000), (2, 256, 4)))
+    return out
+
+
 def config_cases(include_large: bool) -> List[Case]:
     out = [
         Case("cfg_c1", _cfg("c1"), 1000, S.CONFIGS["c1"].rng, S.CONFIGS["c1"].blocks),
@@ -175,7 +207,7 @@ def config_cases(include_large: bool) -> List[Case]:
 
 def all_cases(include_large: bool = False) -> List[Case]:
     return (config_cases(include_large) + _ref_correctness() + _ref_granularity() +
-            _ref_manual() + _edge())
+            _ref_manual() + _edge() + _wide())
 
 
 def by_name(include_large: bool = True):

@@ -208,3 +208,22 @@ def test_cube_threshold_idea_is_exact():
             direct = min(int(math.ceil(ratio(d))), blocks - 1)
             via_tab = int(np.sum(tab < d))
             assert direct == via_tab, (float(bs), float(d))
+
+
+def test_reference_import_name_resolves_to_the_engine():
+    """`import yuezu_fps.yuezu_fps_module as yf` (the reference's name,
+    setup.py:6, test.py:3) gives this engine's module object."""
+    import yuezu_fps.yuezu_fps_module as yf
+    import ns_fps_b200.yuezu_fps_module as m
+    assert yf is m
+    r = yf.make_range(-1, 1, -2, 2, -3, 3, 128, 128, 2)
+    assert (r.x_blocks, r.y_blocks, r.z_blocks) == (128, 128, 2)
+
+
+def test_test_hooks_set_and_reset_without_gpu():
+    capi.set_test_hooks(wait_limit_ns=1_000_000, withhold_cta=3, withhold_step=2,
+                        fail_alloc_device=0)
+    capi.set_test_hooks(reset=True)
+    with pytest.raises(RuntimeError, match="rc=1"):
+        capi.set_test_hooks(wait_limit_ns=10 ** 12)
+    capi.set_test_hooks(reset=True)
