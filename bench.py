@@ -270,14 +270,17 @@ def batch_c5(args, rank: int, world: int, dev, capi, flush, stream):
     torch.cuda.synchronize(dev)
     D.barrier(dev.index)
     samples, ms = 0, 0.0
-    for _ in range(max(1, args.c5_steps)):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        samples += sum(step())
-        b.record(stream)
-        b.synchronize()
-        ms += a.elapsed_time(b)
+    capi.set_profiling(True)
+    with ClockSampler(dev.index) as clk:
+        for _ in range(max(1, args.c5_steps)):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            samples += sum(step())
+            b.record(stream)
+            b.synchronize()
+            ms += a.elapsed_time(b)
+    prof = capi.last_profile()
     steps = max(1, args.c5_steps)
     mine = np.zeros(world)
     mine[rank] = ms / steps
@@ -290,7 +293,10 @@ def batch_c5(args, rank: int, world: int, dev, capi, flush, stream):
     rec = {"workload": "c5", "value": total / steps / (slow / 1e3), "unit": "samples/s",
            "scaling": "strong", "scans": cfg.clouds, "scans_per_gpu": per,
            "ms_per_step": slow, "rank_ms": rank_ms, "slowest_over_fastest": slow / fast,
-           "steps": steps, "warmup": 1}
+           "steps": steps, "warmup": 1,
+           "layout": {"mode": "grid groups" if prof.mode == 3 else "clusters",
+                      "ctas_per_scan": int(prof.ctas_per_cloud)},
+           "clocks": clk.summary()}
     if not args.no_cpu_baseline:
         import oracle
         threads = min(16, os.cpu_count() or 1)

@@ -291,11 +291,17 @@ struct Buffers {
 };
 
 // CTAs per cloud the setup plans for: cluster sizes (one thread-block
-// cluster per cloud), then grid-wide sizes (one cloud over co-resident CTAs).
-constexpr uint32_t kClusterCand[] = {1, 2, 4, 8, 16, 32, 64, 128};
-constexpr int kNumCand = 8;
+// cluster per cloud) first, then for one cloud the grid-wide sizes (one cloud
+// over co-resident CTAs), for a batch the other sizes of CTA groups
+// (groups of co-resident CTAs, each sampling its share of the clouds).
+constexpr uint32_t kSingleCand[] = {1, 2, 4, 8, 16, 32, 64, 128};
+constexpr uint32_t kBatchCand[] = {1, 2, 4, 8, 16, 6, 10, 12, 14};
+constexpr int kNumSingle = 8, kNumBatch = 9;
+static_assert(kNumSingle <= kMaxCand && kNumBatch <= kMaxCand, "plan capacity");
 constexpr int kNumCluster = 5;
 constexpr uint32_t kMaxGridP = 128;
+// CTAs a grid-wide launch may hold (list buffers and counters are sized for it)
+constexpr uint32_t kMaxGridCtas = 256;
 // Points from which one cloud runs on the grid-wide loop even when it fits a
 // cluster.
 constexpr uint32_t kGridMinPoints = NSFPS_GRID_MIN_POINTS;
@@ -333,9 +339,13 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   b.out_count = c.take<uint32_t>(j.B);
   b.out = own_out ? c.take<uint64_t>((size_t)j.B * j.k) : nullptr;
   b.stats = c.take<unsigned long long>(4);
-  b.glist = j.B == 1 ? c.take<uint4>(std::max(rounds_grid_list_bytes(64), rounds_grid_list_bytes(128)) / 16)
-                     : nullptr;
-  b.gbar = j.B == 1 ? c.take<uint32_t>(1) : nullptr;
+  // grid-wide lists and counters: one cloud over 64 or 128 CTAs, or groups of
+  // at most 16 CTAs over at most kMaxGridCtas
+  const size_t glist_bytes =
+      j.B == 1 ? std::max(rounds_grid_list_bytes(64, 1), rounds_grid_list_bytes(128, 1))
+               : rounds_grid_list_bytes(16, kMaxGridCtas / 16);
+  b.glist = c.take<uint4>(glist_bytes / 16);
+  b.gbar = c.take<uint32_t>(kMaxGridCtas);
   return align_up(c.off, 256);
 }
 
@@ -448,8 +458,9 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
                              cudaMemcpyHostToDevice, st));
   NSFPS_CUDA(cudaMemcpyAsync(b.tabs, j.tabs.data(), sizeof(float) * j.tabs.size(),
                              cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(cudaMemcpyAsync(b.cand, kClusterCand, sizeof(kClusterCand),
-                             cudaMemcpyHostToDevice, st));
+  const uint32_t *cand = j.B == 1 ? kSingleCand : kBatchCand;
+  const int ncand = j.B == 1 ? kNumSingle : kNumBatch;
+  NSFPS_CUDA(cudaMemcpyAsync(b.cand, cand, sizeof(uint32_t) * ncand, cudaMemcpyHostToDevice, st));
   NSFPS_CUDA(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
 
   SetupArgs sa{};
@@ -473,14 +484,14 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   sa.loff = b.loff;
   sa.scalars = b.scalars;
   sa.cand = b.cand;
-  sa.cand_host = kClusterCand;
-  sa.ncand = kNumCand;
+  sa.cand_host = cand;
+  sa.ncand = ncand;
   sa.plan = b.plan;
   NSFPS_CUDA(run_setup(sa, st, launches));
 
   uint32_t hplan[3 * kMaxCand] = {};
   uint32_t hscal[kScalarCount] = {};
-  NSFPS_CUDA(cudaMemcpyAsync(hplan, b.plan, sizeof(uint32_t) * 3 * kNumCand,
+  NSFPS_CUDA(cudaMemcpyAsync(hplan, b.plan, sizeof(uint32_t) * 3 * ncand,
                              cudaMemcpyDeviceToHost, st));
   NSFPS_CUDA(cudaMemcpyAsync(hscal, b.scalars, sizeof(hscal), cudaMemcpyDeviceToHost, st));
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
@@ -503,7 +514,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   bool rounds = !j.any_hashed && !g_force_steps.load();
   auto fits = [&](int i, int &m, size_t &bytes) {
     const uint32_t pts = hplan[3 * i], leaves = hplan[3 * i + 1], extra = hplan[3 * i + 2];
-    const uint32_t P = kClusterCand[i];
+    const uint32_t P = cand[i];
     bytes = rounds ? rounds_smem_bytes(pts, leaves, max_tab)
                    : loop_smem_bytes(pts, leaves, extra, max_tab);
     const int cap = rounds ? rounds_max_smem(P) : max_smem;
@@ -522,7 +533,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
         pi = i; m_sel = m; bytes_sel = bytes;
         continue;
       }
-      if ((!rounds && m_sel == 1) || (uint64_t)j.B * kClusterCand[i] > (uint64_t)sms) break;
+      if ((!rounds && m_sel == 1) || (uint64_t)j.B * cand[i] > (uint64_t)sms) break;
       pi = i; m_sel = m; bytes_sel = bytes;
     }
   };
@@ -538,11 +549,14 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   // a single cloud of many points that fits a cluster: over more CTAs its
   // parts are smaller (lighter workers, shorter lists) and it runs faster.
   bool grid = false;
+  uint32_t groups = 1;
   if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&
       (pi < 0 || j.n >= kGridMinPoints)) {
-    for (int i = kNumCluster; i < kNumCand && !grid; ++i) {
-      const uint32_t P = kClusterCand[i];
-      if (P > (uint32_t)sms || P > kMaxGridP || rounds_grid_candidates_per_cta(P) == 0) continue;
+    for (int i = kNumCluster; i < kNumSingle && !grid; ++i) {
+      const uint32_t P = cand[i];
+      // one cloud: 64 or 128 CTAs (32 with 8 candidates each was slower on
+      // c2, 4.89 against 4.16 ms at 64)
+      if (P > (uint32_t)sms || P > kMaxGridP || (P != 64u && P != 128u)) continue;
       const bool was_rounds = rounds;
       rounds = true;
       int m;
@@ -554,6 +568,36 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
       }
     }
   }
+  // A batch whose clouds fit the round loop: the layout that keeps the most
+  // clouds running at once.  A cluster must fit one GPC, so at one CTA per
+  // SM the device holds only some clusters (7 of 16 CTAs on B200, 112 of
+  // 148 SMs); groups of co-resident CTAs (the grid-wide loop, one group per
+  // cloud in turn) have no such limit.
+  if (j.B > 1 && rounds && pi >= 0 && !g_force_steps.load()) {
+    const uint32_t Pc = cand[pi];
+    int force = -1;  // NSFPS_BATCH_GROUP_CTAS: 0 = clusters, P = groups of P CTAs
+    if (const char *v = std::getenv("NSFPS_BATCH_GROUP_CTAS")) force = std::atoi(v);
+    const int cap = force < 0 ? rounds_cluster_capacity(Pc, m_sel, std::max<size_t>(bytes_sel, 16)) : 0;
+    const uint32_t conc_c = cap > 0 ? std::min<uint32_t>(j.B, (uint32_t)cap * 1u) : j.B;
+    int gi = -1;
+    if (force > 0) {
+      for (int i = 0; i < kNumBatch; ++i)
+        if (cand[i] == (uint32_t)force) gi = i;
+    } else if (force < 0 && conc_c < j.B && Pc >= 2) {
+      gi = pi;  // the same CTAs per cloud, more clouds at once
+    }
+    if (gi >= 0) {
+      int m;
+      size_t bytes;
+      const uint32_t P = cand[gi];
+      if (P <= (uint32_t)sms && rounds_grid_candidates_per_cta(P) > 0 && fits(gi, m, bytes)) {
+        pi = gi; m_sel = m; bytes_sel = bytes; grid = true;
+        groups = std::min<uint32_t>(j.B, std::min<uint32_t>((uint32_t)sms, kMaxGridCtas) / P);
+      } else if (force > 0) {
+        return set_error(NSFPS_ERR_UNSUPPORTED, "NSFPS_BATCH_GROUP_CTAS=%d does not fit", force);
+      }
+    }
+  }
   if (pi < 0)
     return set_error(NSFPS_ERR_UNSUPPORTED,
                      "cloud too large for the shared-memory-resident sampler "
@@ -562,7 +606,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   LoopPlan plan{};
   plan.mode = grid ? 1 : 0;
   plan.rounds = rounds ? 1 : 0;
-  plan.P = kClusterCand[pi];
+  plan.P = cand[pi];
   plan.leaves_per_thread = m_sel;
   plan.direct = !j.any_hashed;
   plan.smem_bytes = std::max<size_t>(bytes_sel, 16);
@@ -590,6 +634,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   la.out_count = b.out_count;
   la.scalars = b.scalars;
   la.stats = b.stats;
+  la.groups = grid ? groups : 0;
   la.glist = b.glist;
   la.gbar = b.gbar;
   la.timeout_ns = g_wait_ns.load();

@@ -19,7 +19,7 @@ enum : int {
 constexpr uint32_t kStatusTimeout = 1u;
 constexpr uint32_t kStatusBadPlan = 2u;
 
-constexpr int kMaxCand = 8;
+constexpr int kMaxCand = 16;
 
 // Points from which a single cloud takes the grid-wide round loop (build-time).
 #ifndef NSFPS_GRID_MIN_POINTS
@@ -103,8 +103,9 @@ struct LoopArgs {
   uint32_t *out_count;        // B
   uint32_t *scalars;
   unsigned long long *stats;  // [0] reference-updated points, [1] evaluated
-  uint4 *glist;               // grid-wide rounds: 2 * P published lists (global)
-  uint32_t *gbar;             // grid-wide rounds: arrival counter (starts at 0)
+  uint32_t groups;            // grid-wide rounds: groups of P CTAs in the grid
+  uint4 *glist;               // grid-wide rounds: 2 * P published lists per group (global)
+  uint32_t *gbar;             // grid-wide rounds: one arrival counter per group (start at 0)
   long long timeout_ns;       // limit of every bounded wait
   // test hook: CTA `hold_cta` of cloud 0 does not publish at round / step
   // `hold_step` (-1: never), so that the waits for it run out
@@ -134,10 +135,14 @@ size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab);
 int rounds_max_smem(uint32_t P);
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                        uint32_t &launches);
-// Grid-wide rounds (one cloud over P co-resident CTAs, lists through global
-// memory): candidates per CTA and the bytes of the global list buffers.
+// Grid-wide rounds (groups of P co-resident CTAs, each sampling its share of
+// the clouds, lists through global memory): candidates per CTA (0 when no
+// grid-wide instance exists for P), the bytes of the global list buffers of
+// `groups` groups, and how many clusters of P CTAs the device holds at once
+// (for the choice between the two layouts; 0 when unknown).
 int rounds_grid_candidates_per_cta(uint32_t P);
-size_t rounds_grid_list_bytes(uint32_t P);
+size_t rounds_grid_list_bytes(uint32_t P, uint32_t groups);
+int rounds_cluster_capacity(uint32_t P, int m, size_t smem);
 
 cudaError_t run_loop(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
                      uint32_t &launches);

@@ -230,11 +230,17 @@ __device__ __forceinline__ uint32_t replay_lo(uint32_t rel_pos, uint32_t slot) {
 }
 
 // GRID: the cloud's P CTAs are co-resident but not one cluster; the lists go
-// through global memory (a.glist, by round parity) and a grid barrier (a.gbar)
-// replaces the cluster copies and mbarriers.
-template <int M, int T, bool GRID, int CAP>
+// through global memory (a.glist, by round parity) and a barrier over the P
+// CTAs (an arrival counter in a.gbar) replaces the cluster copies and
+// mbarriers.  The grid holds G groups of P CTAs (G = gridDim.x / P, all
+// co-resident: a cooperative launch); group g samples clouds g, g + G,
+// g + 2G, ... one after the other, each with its own list buffers and
+// counter, so a batch fills every SM whatever clusters the GPU could hold.
+// Without GRID, one cluster of P CTAs samples one cloud.
+template <int M, int T, bool GRID, int CAP, bool BATCH = false>
 __global__ void __launch_bounds__(kRoundThreads, 1)
 fps_rounds_cluster(const LoopArgs a) {
+  static_assert(!BATCH || GRID, "batch groups exchange through global memory");
   constexpr int THREADS = kRoundThreads;
   constexpr int kMaxCands = CAP;
   static_assert(kMaxCands <= 512, "at most 512 candidates (9-bit slots)");
@@ -245,9 +251,13 @@ fps_rounds_cluster(const LoopArgs a) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t P = a.P;
-  const uint32_t cloud = blockIdx.x / P;
+  const uint32_t group = blockIdx.x / P;
   const uint32_t crank = blockIdx.x % P;  // == %cluster_ctarank
   const uint32_t NC = P * T;              // candidates per round
+  // the group's list buffers (2 * P lists, by round parity) and arrival counter
+  constexpr int kListWords = (int)(sizeof(CtaList<T>) / 16);
+  uint4 *const glist = BATCH ? a.glist + (size_t)group * 2u * P * kListWords : a.glist;
+  uint32_t *const gbar = BATCH ? a.gbar + group : a.gbar;
 
   float4 *s_pts = smem;
   float4 *s_lo = s_pts + a.max_pts;    // (lo.xyz, start | count << 16)
@@ -258,6 +268,14 @@ fps_rounds_cluster(const LoopArgs a) {
   using SampleT = std::conditional_t<kMask, MaskedSample, Sample>;
   SampleT *s_samp = reinterpret_cast<SampleT *>(s_tab + ((a.max_tab + 3u) & ~3u));
 
+  uint32_t u_ref = 0, u_eval = 0;
+  bool timed_out = false, bad_any = false;
+  const long long tmo = a.timeout_ns;
+  const int half = lane >> 4, j16 = lane & 15;
+  // rounds this group ran on its earlier clouds: the list slot and counter
+  // target of a round continue across the group's clouds
+  uint32_t round_base = 0;
+  for (uint32_t cloud = group;;) {
   const RangeDev &Rg = a.ranges[a.rid[cloud]];
   const uint32_t n0 = Rg.blocks[0] - 1, n1 = Rg.blocks[1] - 1, n2 = Rg.blocks[2] - 1;
   const bool fast = Rg.fast_cube != 0;
@@ -416,13 +434,15 @@ fps_rounds_cluster(const LoopArgs a) {
 
   const uint32_t tx_bytes = P * (uint32_t)sizeof(CtaList<T>);
   if (tid == 0) {
-    for (int b = 0; b < kListBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
-    fence_mbar_init();
-    for (int b = 0; b < kListBufs; ++b) mbar_arm(smem_u32(&ctl.mbar[b]), tx_bytes);
+    if (!BATCH) {  // (a batch group re-enters here per cloud; it uses no mbarrier)
+      for (int b = 0; b < kListBufs; ++b) mbar_init(smem_u32(&ctl.mbar[b]), 1);
+      fence_mbar_init();
+      for (int b = 0; b < kListBufs; ++b) mbar_arm(smem_u32(&ctl.mbar[b]), tx_bytes);
+    }
     ctl.finished = 0;
   }
   __syncthreads();
-  cluster_sync_all();  // every CTA's mbarriers are armed before any remote write
+  if (!BATCH) cluster_sync_all();  // every CTA's mbarriers are armed before any remote write
 
   // kMask: every replay lane holds the cell boxes of slots lane and 32 + lane
   // (unpacked: x0, x1, y0, y1, z0, z1), for the mask words 0 and 1
@@ -438,11 +458,7 @@ fps_rounds_cluster(const LoopArgs a) {
     rsb[h][4] = bx.x >> 20; rsb[h][5] = bx.y >> 20;
   }
 
-  uint32_t u_ref = 0, u_eval = 0;
   uint32_t it = 1;           // next sample index (sample 0 is point 0)
-  bool timed_out = false;
-  const long long tmo = a.timeout_ns;
-  const int half = lane >> 4, j16 = lane & 15;
 
   // ---- apply queued samples s0 .. s0+nb-1 (nb <= kBatch) to this worker's
   // leaves.  Each point takes min(old, d) over the samples whose cube holds its
@@ -560,8 +576,12 @@ fps_rounds_cluster(const LoopArgs a) {
   };
 
   uint32_t out_n = 0, out_first = 0;  // the round's samples (worker warps)
-  for (uint32_t round = 0;; ++round) {
+  uint32_t round = 0;
+  for (;; ++round) {
     const uint32_t buf = round & (kListBufs - 1);
+    // the group's round (list slot, counter target), numbered on across a
+    // batch group's clouds
+    const uint32_t grnd = BATCH ? round_base + round : round;
 
     // ---- 1a. each worker warp: its T+1 best leaves by leaf maximum, in
     // order (keys are unique: every leaf has its own sorted position)
@@ -734,22 +754,23 @@ fps_rounds_cluster(const LoopArgs a) {
           // arrive there is undefined
           if (lane == 0 && !timed_out) mbar_arm(mb, tx_bytes);
         } else {
-          // ---- publish to global memory, then a grid barrier (bounded).  Slot
-          // (round & 1) is rewritten two rounds later, after every CTA passed
-          // the next barrier, so after every CTA read it.
+          // ---- publish to global memory, then the group's barrier (bounded).
+          // Slot (grnd & 1) is rewritten two rounds later, after every CTA of
+          // the group passed the next barrier, so after every CTA read it;
+          // the group's rounds are numbered on across its clouds.
           __syncwarp();
           constexpr int kWords = (int)(sizeof(CtaList<T>) / 16);
           const uint4 *src = reinterpret_cast<const uint4 *>(&ctl.stage);
-          uint4 *dst = a.glist + ((size_t)(round & 1u) * P + crank) * kWords;
+          uint4 *dst = glist + ((size_t)(grnd & 1u) * P + crank) * kWords;
           if (!hold)
             for (int w = lane; w < kWords; w += 32) __stcg(dst + w, src[w]);
           __syncwarp();  // lane 0's release below covers every lane's stores
           if (lane == 0) {
-            const uint32_t target = (round + 1u) * P;
-            if (!hold) red_release_gpu_add(a.gbar, 1u);
+            const uint32_t target = (grnd + 1u) * P;
+            if (!hold) red_release_gpu_add(gbar, 1u);
             unsigned long long deadline = 0;
             uint32_t polls = 0;
-            while (ld_acquire_gpu(a.gbar) < target) {
+            while (ld_acquire_gpu(gbar) < target) {
               if (polls >= 64u) __nanosleep(64);  // the first polls without backoff
               if ((++polls & 255u) == 0) {
                 const unsigned long long now = globaltimer();
@@ -772,7 +793,7 @@ fps_rounds_cluster(const LoopArgs a) {
         const uint32_t pbase = a.poff[cloud];
         // B* = the largest bound, in the replay key's encoding
         const CtaList<T> *lists =
-            GRID ? reinterpret_cast<const CtaList<T> *>(a.glist) + (size_t)(round & 1u) * P
+            GRID ? reinterpret_cast<const CtaList<T> *>(glist) + (size_t)(grnd & 1u) * P
                  : ctl.list[buf];
         // this lane's candidates, loaded together with the bounds (one
         // round trip to L2 in the grid-wide loop)
@@ -1105,12 +1126,20 @@ fps_rounds_cluster(const LoopArgs a) {
         a.out_rank[(uint64_t)cloud * a.k + out_first + s2] = s_samp[s2].c.w;
     if (ctl.finished) break;
   }
+  // ---- this cloud's epilogue
+  if (warp == 0 && lane == 0 && crank == 0) a.out_count[cloud] = it;
+  bad_any = bad_any || bad;
+  if (!BATCH) break;  // one cloud per cluster / per single-cloud grid
+  round_base += round + 1u;
+  cloud += gridDim.x / P;
+  // a group whose wait ran out stops (its other CTAs' next waits run out too)
+  if (__syncthreads_or(timed_out ? 1 : 0) || cloud >= a.B) break;
+  }  // clouds
 
   // ---- epilogue
   if (lane == 0) {
-    const uint32_t status = (timed_out ? kStatusTimeout : 0u) | (bad ? kStatusBadPlan : 0u);
+    const uint32_t status = (timed_out ? kStatusTimeout : 0u) | (bad_any ? kStatusBadPlan : 0u);
     if (status) atomicOr(a.scalars + kScalarStatus, status);
-    if (warp == 0 && crank == 0) a.out_count[cloud] = it;
   }
   {
     unsigned long long r64 = u_ref, e64 = u_eval;
@@ -1139,9 +1168,9 @@ fps_rounds_cluster(const LoopArgs a) {
   }
 }
 
-template <int M, int T, bool GRID, int CAP>
+template <int M, int T, bool GRID, int CAP, bool BATCH = false>
 cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
-  auto kern = fps_rounds_cluster<M, T, GRID, CAP>;
+  auto kern = fps_rounds_cluster<M, T, GRID, CAP, BATCH>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err) return err;
@@ -1150,12 +1179,12 @@ cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
     if (err) return err;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.B * a.P, 1, 1);
+  cfg.gridDim = dim3((BATCH ? a.groups : a.B) * a.P, 1, 1);
   cfg.blockDim = dim3(kRoundThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  if (GRID) {  // every CTA co-resident (the grid barrier needs it), or no launch
+  if (GRID) {  // every CTA co-resident (the groups' barriers need it), or no launch
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
   } else {
@@ -1169,18 +1198,18 @@ cudaError_t launch_rounds(const LoopArgs &a, size_t smem, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int T, bool GRID, int CAP>
+template <int T, bool GRID, int CAP, bool BATCH = false>
 cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t st) {
   switch (m) {
-    case 1: return launch_rounds<1, T, GRID, CAP>(a, smem, st);
-    case 2: return launch_rounds<2, T, GRID, CAP>(a, smem, st);
-    case 3: return launch_rounds<3, T, GRID, CAP>(a, smem, st);
-    case 4: return launch_rounds<4, T, GRID, CAP>(a, smem, st);
+    case 1: return launch_rounds<1, T, GRID, CAP, BATCH>(a, smem, st);
+    case 2: return launch_rounds<2, T, GRID, CAP, BATCH>(a, smem, st);
+    case 3: return launch_rounds<3, T, GRID, CAP, BATCH>(a, smem, st);
+    case 4: return launch_rounds<4, T, GRID, CAP, BATCH>(a, smem, st);
     case 6: return kMaxLeavesPerThread >= 6
-                       ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T, GRID, CAP>(a, smem, st)
+                       ? launch_rounds<(kMaxLeavesPerThread >= 6 ? 6 : 1), T, GRID, CAP, BATCH>(a, smem, st)
                        : cudaErrorInvalidValue;
     case 8: return kMaxLeavesPerThread >= 8
-                       ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T, GRID, CAP>(a, smem, st)
+                       ? launch_rounds<(kMaxLeavesPerThread >= 8 ? 8 : 1), T, GRID, CAP, BATCH>(a, smem, st)
                        : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
@@ -1191,8 +1220,12 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
 // the largest CTA bound; more candidates per CTA lower that bound but cost
 // every step more work: on c2 (P = 64) 4, 6 and 8 per CTA gave 4.160, 4.149
 // and 4.19 ms, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
-constexpr int grid_t(uint32_t P) { return P == 64u ? 6 : (P == 128u ? 4 : 0); }
-constexpr int grid_cap(uint32_t P) { return (int)P * grid_t(P); }
+// Groups of at most 32 CTAs (batches) publish kRoundT each, as a cluster does.
+constexpr int grid_t(uint32_t P) {
+  return P == 64u ? 6 : (P == 128u ? 4 : (P <= 32u ? kRoundT : 0));
+}
+constexpr int grid_cap(uint32_t P) { return P == 64u || P == 128u ? (int)P * grid_t(P) : kClusterCap; }
+static_assert(32 * kRoundT <= kClusterCap, "groups of up to 32 CTAs fit the cluster capacity");
 
 }  // namespace
 
@@ -1226,9 +1259,49 @@ int rounds_grid_candidates_per_cta(uint32_t P) {
   return grid_t(P);
 }
 
-size_t rounds_grid_list_bytes(uint32_t P) {
-  return P == 64u ? 2 * (size_t)P * sizeof(CtaList<grid_t(64)>)
-                  : (P == 128u ? 2 * (size_t)P * sizeof(CtaList<grid_t(128)>) : 0);
+size_t rounds_grid_list_bytes(uint32_t P, uint32_t groups) {
+  const size_t list = P == 64u    ? sizeof(CtaList<grid_t(64)>)
+                      : P == 128u ? sizeof(CtaList<grid_t(128)>)
+                                  : sizeof(CtaList<kRoundT>);
+  return grid_t(P) ? (size_t)groups * 2 * P * list : 0;
+}
+
+int rounds_cluster_capacity(uint32_t P, int m, size_t smem) {
+  // clusters of P CTAs of the round kernel the device holds at once (a
+  // cluster must fit one GPC: on B200 7 clusters of 16 CTAs at one CTA per SM)
+  if (P == 0 || P > (uint32_t)kMaxClusterP) return 0;
+  const void *kern = nullptr;
+  switch (m) {
+    case 1: kern = (const void *)fps_rounds_cluster<1, kRoundT, false, kClusterCap>; break;
+    case 2: kern = (const void *)fps_rounds_cluster<2, kRoundT, false, kClusterCap>; break;
+    case 3: kern = (const void *)fps_rounds_cluster<3, kRoundT, false, kClusterCap>; break;
+    case 4: kern = (const void *)fps_rounds_cluster<4, kRoundT, false, kClusterCap>; break;
+    case 6: kern = (const void *)fps_rounds_cluster<6, kRoundT, false, kClusterCap>; break;
+    case 8: kern = (const void *)fps_rounds_cluster<8, kRoundT, false, kClusterCap>; break;
+    default: return 0;
+  }
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+      (P > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1))) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P, 1, 1);
+  cfg.blockDim = dim3(kRoundThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = P;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
@@ -1236,13 +1309,17 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
   if (!plan.direct) return cudaErrorInvalidValue;
   cudaError_t err;
   if (plan.mode == 1) {
-    if (a.B != 1 || !a.glist || !a.gbar || rounds_grid_candidates_per_cta(a.P) == 0)
-      return cudaErrorInvalidValue;
-    if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t), st))) return err;
-    err = a.P == 64u ? launch_rounds_m<grid_t(64), true, grid_cap(64)>(a, plan.leaves_per_thread,
-                                                                         plan.smem_bytes, st)
-                     : launch_rounds_m<grid_t(128), true, grid_cap(128)>(a, plan.leaves_per_thread,
-                                                                           plan.smem_bytes, st);
+    if (!a.glist || !a.gbar || rounds_grid_candidates_per_cta(a.P) == 0) return cudaErrorInvalidValue;
+    const int m = plan.leaves_per_thread;
+    if (a.B == 1 && (a.P == 64u || a.P == 128u)) {  // one cloud over 64 or 128 CTAs
+      if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t), st))) return err;
+      err = a.P == 64u ? launch_rounds_m<grid_t(64), true, grid_cap(64)>(a, m, plan.smem_bytes, st)
+                       : launch_rounds_m<grid_t(128), true, grid_cap(128)>(a, m, plan.smem_bytes, st);
+    } else {  // a batch over groups of P CTAs
+      if (a.groups == 0 || a.groups > a.B || a.P > 32u) return cudaErrorInvalidValue;
+      if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t) * a.groups, st))) return err;
+      err = launch_rounds_m<kRoundT, true, kClusterCap, true>(a, m, plan.smem_bytes, st);
+    }
   } else {
     if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
     err = launch_rounds_m<kRoundT, false, kClusterCap>(a, plan.leaves_per_thread, plan.smem_bytes, st);

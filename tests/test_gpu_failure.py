@@ -126,3 +126,24 @@ def test_sharder_worker_failure_is_reported_then_recovers():
     got = capi.fps_batched(clouds, cfg.k, cfg.rng, cfg.blocks, devices=devs)
     for i, cl in enumerate(clouds):
         np.testing.assert_array_equal(got[i], oracle.fps(cl, cfg.k, cfg.rng, cfg.blocks))
+
+
+def test_withheld_list_in_cta_groups_times_out_and_recovers():
+    """Groups of 4 CTAs over more clouds than groups: group 0 withholds a list
+    on its first cloud; its waits run out while the other groups finish; the
+    call reports the timeout and the next call is exact."""
+    import os
+    cfg = S.CONFIGS["c3"]
+    clouds = [S.sphere_cube_cloud(4096, seed=70 + i) for i in range(40)]
+    k = 500
+    os.environ["NSFPS_BATCH_GROUP_CTAS"] = "4"
+    try:
+        capi.set_test_hooks(wait_limit_ns=WAIT_NS, withhold_cta=2, withhold_step=1)
+        with pytest.raises(RuntimeError, match=f"rc={capi.ERR_TIMEOUT}.*timed out"):
+            capi.fps_batched(clouds, k, cfg.rng, cfg.blocks)
+        capi.set_test_hooks(reset=True)
+        got = capi.fps_batched(clouds, k, cfg.rng, cfg.blocks)
+    finally:
+        os.environ.pop("NSFPS_BATCH_GROUP_CTAS", None)
+    for i in (0, 1, 37, 39):
+        np.testing.assert_array_equal(got[i], oracle.fps(clouds[i], k, cfg.rng, cfg.blocks))

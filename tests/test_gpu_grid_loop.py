@@ -99,3 +99,63 @@ def test_batched_scans_large_parts_match_oracle():
     for i, cl in enumerate(clouds):
         exp = oracle.fps(cl, k, cfg.rng, cfg.blocks)
         assert np.array_equal(got[i], exp), f"scan {i}"
+
+
+def _batch_profiled(clouds, k, rng, blocks, force=None):
+    import os
+    old = os.environ.get("NSFPS_BATCH_GROUP_CTAS")
+    if force is not None:
+        os.environ["NSFPS_BATCH_GROUP_CTAS"] = str(force)
+    capi.set_profiling(True)
+    try:
+        got = capi.fps_batched(clouds, k, rng, blocks)
+        return got, capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+        if force is not None:
+            if old is None:
+                os.environ.pop("NSFPS_BATCH_GROUP_CTAS", None)
+            else:
+                os.environ["NSFPS_BATCH_GROUP_CTAS"] = old
+
+
+def test_batch_of_scans_runs_on_cta_groups():
+    """More scans than the device holds clusters of 16 CTAs (7 on B200): the
+    batch runs on groups of 16 co-resident CTAs, each group sampling its
+    scans one after the other, with lists through global memory."""
+    from ns_fps_b200 import synthetic as S
+    cfg = S.CONFIGS["c5"]
+    clouds = S.make("c5", seed=500, count=12)
+    k = 3000
+    got, prof = _batch_profiled(clouds, k, cfg.rng, cfg.blocks)
+    assert prof.mode == MODE_GRID and prof.ctas_per_cloud == 16, (prof.mode, prof.ctas_per_cloud)
+    for i in (0, 1, 9, 10, 11):  # groups 0..2 take two scans each
+        assert np.array_equal(got[i], oracle.fps(clouds[i], k, cfg.rng, cfg.blocks)), f"scan {i}"
+
+
+def test_cta_groups_loop_over_many_clouds_of_mixed_sizes_and_ranges():
+    """Forced groups of 4 CTAs over 44 clouds (more than the 37 groups the
+    device holds): groups take several clouds in turn, each with its own
+    range and size."""
+    rs = np.random.RandomState(61)
+    clouds, bounds, blocks = [], [], []
+    for i in range(44):
+        n = int(rs.choice([701, 800, 5000, 16384]))
+        p = (rs.rand(n, 3) * rs.uniform(1, 50, 3)).astype(np.float32)
+        clouds.append(p)
+        lo, hi = p.min(0) - 1e-3, p.max(0) + 1e-3
+        bounds.append((lo[0], hi[0], lo[1], hi[1], lo[2], hi[2]))
+        blocks.append(tuple(int(v) for v in rs.choice([4, 8, 16, 32], 3)))
+    k = 700
+    import os
+    os.environ["NSFPS_BATCH_GROUP_CTAS"] = "4"
+    capi.set_profiling(True)
+    try:
+        got = capi.fps_batched(clouds, k, bounds, blocks, per_cloud=True)
+        prof = capi.last_profile()
+    finally:
+        capi.set_profiling(False)
+        os.environ.pop("NSFPS_BATCH_GROUP_CTAS", None)
+    assert prof.mode == MODE_GRID and prof.ctas_per_cloud == 4
+    for i, cl in enumerate(clouds):
+        assert np.array_equal(got[i], oracle.fps(cl, k, bounds[i], blocks[i])), f"cloud {i} n={len(cl)}"
