@@ -202,16 +202,113 @@ int range_info(const nsfps_range &r, nsfps_range_info *info) {
 // ------------------------------------------------------- device contexts
 namespace {
 
+// The setup pipeline of one call shape (its SetupArgs: sizes and workspace
+// pointers), captured once as a CUDA graph and replayed by later calls of
+// the same shape: one launch instead of ~25 small ones.
+struct SetupGraph {
+  SetupArgs args;
+  cudaGraphExec_t exec = nullptr;
+  uint32_t launches = 0;
+  uint64_t used = 0;
+};
+constexpr size_t kSetupGraphs = 8;
+
 struct DeviceCtx {
   std::mutex mu;
   int device = -1;
   cudaStream_t stream = nullptr;
+  cudaStream_t capture = nullptr;  // private stream the setup graphs are captured on
   void *ws = nullptr;
   size_t ws_bytes = 0;
   cudaEvent_t ev[4] = {};
   bool ready = false;
   bool fixed = false;  // the workspace is the static scratch array: never (re)allocated
+  std::vector<SetupGraph> graphs;
+  uint64_t graph_clock = 0;
+  // host staging of a call's small uploads and downloads: pinned (one
+  // asynchronous copy each way), or a plain vector for the static context,
+  // which allocates nothing on the device side
+  void *pin = nullptr;
+  size_t pin_bytes = 0;
+  std::vector<unsigned char> pageable;
 };
+
+// Host staging area of at least `bytes` for ctx (pinned unless the context is
+// the static one); nullptr when it cannot be had.
+unsigned char *staging(DeviceCtx *ctx, size_t bytes) {
+  if (ctx->fixed) {
+    if (ctx->pageable.size() < bytes) ctx->pageable.resize(bytes);
+    return ctx->pageable.data();
+  }
+  if (ctx->pin_bytes < bytes) {
+    if (ctx->pin) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFreeHost(ctx->pin);
+      ctx->pin = nullptr;
+      ctx->pin_bytes = 0;
+    }
+    const size_t want = std::max<size_t>(bytes + bytes / 2, 64 << 10);
+    if (cudaMallocHost(&ctx->pin, want) != cudaSuccess) {
+      cudaGetLastError();
+      ctx->pin = nullptr;
+      return nullptr;
+    }
+    ctx->pin_bytes = want;
+  }
+  return (unsigned char *)ctx->pin;
+}
+
+void drop_setup_graphs(DeviceCtx *ctx) {
+  for (SetupGraph &g : ctx->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  ctx->graphs.clear();
+}
+
+// Runs the setup pipeline on `st`, from a cached graph of this shape when
+// there is one (captured now when there is not).  The static context never
+// captures: instantiating a graph may allocate.
+cudaError_t run_setup_cached(DeviceCtx *ctx, const SetupArgs &sa, cudaStream_t st,
+                             uint32_t &launches) {
+  if (ctx->fixed) return run_setup(sa, st, launches);
+  SetupGraph *hit = nullptr;
+  for (SetupGraph &g : ctx->graphs)
+    if (std::memcmp(&g.args, &sa, sizeof(SetupArgs)) == 0) hit = &g;
+  if (!hit) {
+    cudaError_t e = cudaSuccess;
+    if (!ctx->capture) e = cudaStreamCreateWithFlags(&ctx->capture, cudaStreamNonBlocking);
+    cudaGraph_t graph = nullptr;
+    uint32_t l = 0;
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(ctx->capture, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      const cudaError_t er = run_setup(sa, ctx->capture, l);
+      e = cudaStreamEndCapture(ctx->capture, &graph);
+      if (e == cudaSuccess) e = er;
+    }
+    cudaGraphExec_t exec = nullptr;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {  // no graph: launch the pipeline directly
+      cudaGetLastError();
+      return run_setup(sa, st, launches);
+    }
+    if (ctx->graphs.size() >= kSetupGraphs) {  // evict the least recently used
+      size_t old = 0;
+      for (size_t i = 1; i < ctx->graphs.size(); ++i)
+        if (ctx->graphs[i].used < ctx->graphs[old].used) old = i;
+      cudaGraphExecDestroy(ctx->graphs[old].exec);
+      ctx->graphs.erase(ctx->graphs.begin() + (long)old);
+    }
+    SetupGraph g;
+    g.args = sa;
+    g.exec = exec;
+    g.launches = l;
+    ctx->graphs.push_back(g);
+    hit = &ctx->graphs.back();
+  }
+  hit->used = ++ctx->graph_clock;
+  launches += hit->launches;
+  return cudaGraphLaunch(hit->exec, st);
+}
 
 constexpr int kMaxDevices = 64;
 DeviceCtx g_ctx[kMaxDevices];
@@ -276,6 +373,8 @@ struct Job {
 };
 
 struct Buffers {
+  unsigned char *params;  // poff | rid | boff | ranges | tabs | cand, uploaded as one copy
+  unsigned char *ctrl;    // scalars | stats | plan | out_count, downloaded as one copy
   float *xyz;
   uint32_t *keys0, *vals0, *keys1, *vals1, *hist, *partial, *perm, *tmp0, *tmp1;
   float4 *pts, *leaf_lo, *leaf_hi;
@@ -306,6 +405,35 @@ constexpr uint32_t kMaxGridCtas = 256;
 // cluster.
 constexpr uint32_t kGridMinPoints = NSFPS_GRID_MIN_POINTS;
 
+// Byte offsets of a job's small per-call inputs inside the params block, and
+// of the counters and results inside the control block.
+struct ParamLayout {
+  size_t poff, rid, boff, ranges, tabs, cand, bytes;
+};
+ParamLayout param_layout(const Job &j) {
+  ParamLayout L{};
+  size_t o = 0;
+  auto put = [&](size_t sz) {
+    const size_t at = o;
+    o = align_up(o + std::max<size_t>(sz, 1), 16);
+    return at;
+  };
+  L.poff = put(4 * ((size_t)j.B + 1));
+  L.rid = put(4 * (size_t)j.B);
+  L.boff = put(4 * (size_t)j.B);
+  L.ranges = put(sizeof(RangeDev) * j.ranges.size());
+  L.tabs = put(sizeof(float) * j.tabs.size());
+  L.cand = put(4 * (size_t)kMaxCand);
+  L.bytes = o;
+  return L;
+}
+constexpr size_t kCtrlScalars = 0;                                   // kScalarCount uint32
+constexpr size_t kCtrlStats = 32;                                    // 4 x uint64
+constexpr size_t kCtrlPlan = 64;                                     // 3 * kMaxCand uint32
+constexpr size_t kCtrlCount = kCtrlPlan + 4 * 3 * kMaxCand;          // B uint32
+static_assert(4 * kScalarCount <= kCtrlStats, "control block layout");
+size_t ctrl_bytes(const Job &j) { return kCtrlCount + 4 * (size_t)j.B; }
+
 size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   const size_t n = j.n;
   const size_t tiles = radix_tiles(j.n);
@@ -327,18 +455,21 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   b.leaf_md = c.take<float>(n);
   b.leaf_pre = j.any_hashed ? c.take<uint32_t>(n * kMaxPreimages) : nullptr;
   b.loff = c.take<uint32_t>(j.B + 1);
-  b.poff = c.take<uint32_t>(j.B + 1);
-  b.rid = c.take<uint32_t>(j.B);
-  b.boff = c.take<uint32_t>(j.B);
-  b.ranges = c.take<RangeDev>(j.ranges.size());
-  b.tabs = c.take<float>(j.tabs.size());
-  b.scalars = c.take<uint32_t>(kScalarCount);
-  b.plan = c.take<uint32_t>(3 * kMaxCand);
-  b.cand = c.take<uint32_t>(kMaxCand);
+  const ParamLayout L = param_layout(j);
+  b.params = c.take<unsigned char>(L.bytes);
+  b.poff = (uint32_t *)(b.params ? b.params + L.poff : nullptr);
+  b.rid = (uint32_t *)(b.params ? b.params + L.rid : nullptr);
+  b.boff = (uint32_t *)(b.params ? b.params + L.boff : nullptr);
+  b.ranges = (RangeDev *)(b.params ? b.params + L.ranges : nullptr);
+  b.tabs = (float *)(b.params ? b.params + L.tabs : nullptr);
+  b.cand = (uint32_t *)(b.params ? b.params + L.cand : nullptr);
+  b.ctrl = c.take<unsigned char>(ctrl_bytes(j));
+  b.scalars = (uint32_t *)(b.ctrl ? b.ctrl + kCtrlScalars : nullptr);
+  b.stats = (unsigned long long *)(b.ctrl ? b.ctrl + kCtrlStats : nullptr);
+  b.plan = (uint32_t *)(b.ctrl ? b.ctrl + kCtrlPlan : nullptr);
+  b.out_count = (uint32_t *)(b.ctrl ? b.ctrl + kCtrlCount : nullptr);
   b.out_rank = c.take<uint32_t>((size_t)j.B * j.k);
-  b.out_count = c.take<uint32_t>(j.B);
   b.out = own_out ? c.take<uint64_t>((size_t)j.B * j.k) : nullptr;
-  b.stats = c.take<unsigned long long>(4);
   // grid-wide lists and counters: one cloud over 64 or 128 CTAs, or groups of
   // at most 16 CTAs over at most kMaxGridCtas
   const size_t glist_bytes =
@@ -363,6 +494,7 @@ int ensure_ws(DeviceCtx *ctx, size_t bytes) {
                      bytes, ctx->ws_bytes);
   if (ctx->ws) {
     cudaStreamSynchronize(ctx->stream);
+    drop_setup_graphs(ctx);  // they point into the old workspace
     cudaFree(ctx->ws);
     ctx->ws = nullptr;
     ctx->ws_bytes = 0;
@@ -451,19 +583,25 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     }
     d_xyz = b.xyz;
   }
-  NSFPS_CUDA(cudaMemcpyAsync(b.poff, j.poff.data(), 4 * (j.B + 1), cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(cudaMemcpyAsync(b.rid, j.rid.data(), 4 * j.B, cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(cudaMemcpyAsync(b.boff, j.boff.data(), 4 * j.B, cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(cudaMemcpyAsync(b.ranges, j.ranges.data(), sizeof(RangeDev) * j.ranges.size(),
-                             cudaMemcpyHostToDevice, st));
-  NSFPS_CUDA(cudaMemcpyAsync(b.tabs, j.tabs.data(), sizeof(float) * j.tabs.size(),
-                             cudaMemcpyHostToDevice, st));
+  // the call's small inputs, staged on the host and uploaded as one copy
   const uint32_t *cand = j.B == 1 ? kSingleCand : kBatchCand;
   const int ncand = j.B == 1 ? kNumSingle : kNumBatch;
-  NSFPS_CUDA(cudaMemcpyAsync(b.cand, cand, sizeof(uint32_t) * ncand, cudaMemcpyHostToDevice, st));
+  const ParamLayout L = param_layout(j);
+  const size_t cbytes = ctrl_bytes(j);
+  unsigned char *hs = staging(ctx, std::max(L.bytes, cbytes));
+  if (!hs) return set_error(NSFPS_ERR_OOM, "host staging buffer of %zu bytes unavailable",
+                            std::max(L.bytes, cbytes));
+  std::memcpy(hs + L.poff, j.poff.data(), 4 * ((size_t)j.B + 1));
+  std::memcpy(hs + L.rid, j.rid.data(), 4 * (size_t)j.B);
+  std::memcpy(hs + L.boff, j.boff.data(), 4 * (size_t)j.B);
+  std::memcpy(hs + L.ranges, j.ranges.data(), sizeof(RangeDev) * j.ranges.size());
+  std::memcpy(hs + L.tabs, j.tabs.data(), sizeof(float) * j.tabs.size());
+  std::memcpy(hs + L.cand, cand, sizeof(uint32_t) * ncand);
+  NSFPS_CUDA(cudaMemcpyAsync(b.params, hs, L.bytes, cudaMemcpyHostToDevice, st));
   NSFPS_CUDA(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
 
-  SetupArgs sa{};
+  SetupArgs sa;
+  std::memset(&sa, 0, sizeof(sa));  // compared bytewise by the graph cache
   sa.n = j.n;
   sa.B = j.B;
   sa.max_key = (uint32_t)(j.total_buckets - 1);
@@ -487,15 +625,17 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   sa.cand_host = cand;
   sa.ncand = ncand;
   sa.plan = b.plan;
-  NSFPS_CUDA(run_setup(sa, st, launches));
+  NSFPS_CUDA(run_setup_cached(ctx, sa, st, launches));
 
+  // scalars, stats and plan come back as one copy (the staging buffer's
+  // upload was issued before on the same stream, so it has been read)
   uint32_t hplan[3 * kMaxCand] = {};
   uint32_t hscal[kScalarCount] = {};
-  NSFPS_CUDA(cudaMemcpyAsync(hplan, b.plan, sizeof(uint32_t) * 3 * ncand,
-                             cudaMemcpyDeviceToHost, st));
-  NSFPS_CUDA(cudaMemcpyAsync(hscal, b.scalars, sizeof(hscal), cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaMemcpyAsync(hs, b.ctrl, kCtrlCount, cudaMemcpyDeviceToHost, st));
   if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
   NSFPS_CUDA(cudaStreamSynchronize(st));
+  std::memcpy(hscal, hs + kCtrlScalars, sizeof(hscal));
+  std::memcpy(hplan, hs + kCtrlPlan, sizeof(uint32_t) * 3 * ncand);
 
   // CTAs per cloud: the smallest count whose largest part fits in shared
   // memory; then, while every cloud still gets its own SMs, keep doubling it:
@@ -648,15 +788,16 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
                           launches));
   lens.assign(j.B, 0);
   unsigned long long hstats[4] = {};
-  NSFPS_CUDA(cudaMemcpyAsync(lens.data(), b.out_count, 4 * j.B, cudaMemcpyDeviceToHost, st));
-  NSFPS_CUDA(cudaMemcpyAsync(hscal, b.scalars, sizeof(hscal), cudaMemcpyDeviceToHost, st));
-  NSFPS_CUDA(cudaMemcpyAsync(hstats, b.stats, sizeof(hstats), cudaMemcpyDeviceToHost, st));
+  NSFPS_CUDA(cudaMemcpyAsync(hs, b.ctrl, cbytes, cudaMemcpyDeviceToHost, st));
   if (h_out) {
     h_out->resize((size_t)j.B * j.k);
     NSFPS_CUDA(cudaMemcpyAsync(h_out->data(), d_out, sizeof(uint64_t) * j.B * (size_t)j.k,
                                cudaMemcpyDeviceToHost, st));
   }
   NSFPS_CUDA(cudaStreamSynchronize(st));
+  std::memcpy(hscal, hs + kCtrlScalars, sizeof(hscal));
+  std::memcpy(hstats, hs + kCtrlStats, sizeof(hstats));
+  std::memcpy(lens.data(), hs + kCtrlCount, 4 * (size_t)j.B);
   if (hscal[kScalarStatus] & kStatusTimeout)
     return set_error(NSFPS_ERR_TIMEOUT, "sampling kernel: a bounded wait timed out");
   if (hscal[kScalarStatus] & kStatusBadPlan)
