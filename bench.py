@@ -59,11 +59,12 @@ L2_NOTE = "GPU arm: 256 MiB L2 flush between steps, outside the timed window"
 SMEM_BYTES_PER_CLK = 128
 
 
-def config_dict(name: str):
+def config_dict(name: str, limit: int = 0):
     """The workload as both arms describe it (identical dicts)."""
     cfg = S.CONFIGS[name]
+    clouds = min(cfg.clouds, limit) if limit > 0 else cfg.clouds
     return {"workload": name, "points": cfg.n, "k": cfg.k, "blocks": list(cfg.blocks),
-            "range": list(cfg.rng), "clouds": cfg.clouds, "l2": L2_NOTE}
+            "range": list(cfg.rng), "clouds": clouds, "l2": L2_NOTE}
 
 
 def parse():
@@ -77,6 +78,9 @@ def parse():
     ap.add_argument("--no-batch-c5", action="store_true",
                     help="skip the 256-scan batch sub-record")
     ap.add_argument("--c5-steps", type=int, default=2, help="timed steps of the batch_c5 record")
+    ap.add_argument("--clouds", type=int, default=0,
+                    help="c3/c5: sample only this many clouds of the batch (small cases "
+                         "for profiling; the bench line then names the count)")
     ap.add_argument("--path", choices=["fps", "group"], default="fps",
                     help="fps: the sampler (default); group: the ball query after it")
     ap.add_argument("--radius", type=float, default=0.5, help="--path group: ball radius")
@@ -84,7 +88,7 @@ def parse():
     return ap.parse_args()
 
 
-def workload_clouds(name: str, rank: int, world: int):
+def workload_clouds(name: str, rank: int, world: int, limit: int = 0):
     """The clouds this rank samples every step, and a description."""
     cfg = S.CONFIGS[name]
     if name in ("c1", "c2", "c4"):
@@ -92,7 +96,7 @@ def workload_clouds(name: str, rank: int, world: int):
         scaling = "weak"
         per = 1
     else:
-        total = cfg.clouds
+        total = min(cfg.clouds, limit) if limit > 0 else cfg.clouds
         idx = D.shard_indices(total, rank, world)
         if name == "c3":
             clouds = [S.sphere_cube_cloud(cfg.n, seed=i) for i in idx]
@@ -215,7 +219,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     import oracle
-    cfg, clouds, scaling, per = workload_clouds(args.workload, 0, 1)
+    cfg, clouds, scaling, per = workload_clouds(args.workload, 0, 1, args.clouds)
     if args.workload in ("c3", "c5"):
         clouds = clouds[: max(1, min(len(clouds), os.cpu_count() or 1))]
     threads = len(clouds)
@@ -239,7 +243,7 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args.workload), "clouds_per_step": len(clouds),
+        "config": config_dict(args.workload, args.clouds), "clouds_per_step": len(clouds),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": kind,
                          "sample": f"{len(clouds)} whole cloud(s) per step, {threads} thread(s)"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
@@ -297,6 +301,24 @@ def batch_c5(args, rank: int, world: int, dev, capi, flush, stream):
            "layout": {"mode": "grid groups" if prof.mode == 3 else "clusters",
                       "ctas_per_scan": int(prof.ctas_per_cloud)},
            "clocks": clk.summary()}
+    # roofline of the batch's sampling-loop launch on rank 0 (the last step):
+    # algorithmic bytes 12 N + 20 sum_i u_i over its scans, over the launch's
+    # event-timed duration; DRAM traffic scaled from the committed capture of
+    # 9 scans (each scan's part is read once, so traffic grows with the scans)
+    n_pts = float(offsets[-1])
+    alg = 12.0 * n_pts + 20.0 * float(prof.ref_points_updated)
+    peak, peak_kind = measured_peaks()
+    t9 = profiled_traffic("c5x9")
+    achieved = alg / (prof.loop_ms / 1e3) / 1e9
+    rec["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                       "frac": achieved / peak, "peak_source": peak_kind,
+                       "traffic": t9 * len(clouds) / 9.0 if t9 else None,
+                       "kernel": "fps_rounds_cluster (batch groups)" if prof.mode == 3
+                                 else "fps_rounds_cluster (clusters)",
+                       "algorithmic_bytes_per_launch": alg,
+                       "kernel_ms_per_launch": float(prof.loop_ms),
+                       "operative_bound": "latency and worker throughput: each scan's serial "
+                                          "step chain; the scans are shared-memory resident"}
     if not args.no_cpu_baseline:
         import oracle
         threads = min(16, os.cpu_count() or 1)
@@ -326,7 +348,7 @@ def run_ours(args):
     D.init("nccl", timeout_s=300)
     from ns_fps_b200 import capi
 
-    cfg, clouds, scaling, per = workload_clouds(args.workload, rank, world)
+    cfg, clouds, scaling, per = workload_clouds(args.workload, rank, world, args.clouds)
     k = cfg.k
     offsets = np.zeros(len(clouds) + 1, dtype=np.int64)
     offsets[1:] = np.cumsum([c.shape[0] for c in clouds])
@@ -424,7 +446,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_dict(args.workload), "clouds_per_gpu": len(clouds),
+            "config": config_dict(args.workload, args.clouds), "clouds_per_gpu": len(clouds),
             "ms_per_scan": my_ms / args.steps / max(len(clouds), 1) if per == 1 else None,
             "us_per_iteration": (loop_ms / args.steps) * 1e3 / max(iters, 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
