@@ -510,6 +510,55 @@ int ensure_ws(DeviceCtx *ctx, size_t bytes) {
   return NSFPS_OK;
 }
 
+// The derived range and its cube threshold tables, cached per range: the
+// tables take one bisection over float bit patterns per block boundary
+// (15-50 us per call on the bench configs), and callers repeat their ranges.
+struct RangeCacheEntry {
+  nsfps_range key;
+  RangeDev dev;               // tab_off relative to `tabs`
+  std::vector<float> tabs;
+  uint64_t used = 0;
+};
+constexpr size_t kRangeCache = 32;
+std::mutex g_range_mu;
+std::vector<RangeCacheEntry> g_range_cache;
+uint64_t g_range_clock = 0;
+
+// range_to_dev + cube_thresholds of r, appending its tables to `pool`.
+int range_with_tables(const nsfps_range &r, RangeDev &out, std::vector<float> &pool) {
+  {
+    std::lock_guard<std::mutex> lk(g_range_mu);
+    for (RangeCacheEntry &e : g_range_cache)
+      if (std::memcmp(&e.key, &r, sizeof(nsfps_range)) == 0) {
+        e.used = ++g_range_clock;
+        out = e.dev;
+        const uint32_t base = (uint32_t)pool.size();
+        for (int a = 0; a < 3; ++a) out.tab_off[a] += base;
+        pool.insert(pool.end(), e.tabs.begin(), e.tabs.end());
+        return NSFPS_OK;
+      }
+  }
+  RangeCacheEntry e;
+  e.key = r;
+  int rc = range_to_dev(r, &e.dev, nullptr);
+  if (rc) return rc;
+  cube_thresholds(e.dev, e.tabs);  // tab_off relative to e.tabs
+  out = e.dev;
+  const uint32_t base = (uint32_t)pool.size();
+  for (int a = 0; a < 3; ++a) out.tab_off[a] += base;
+  pool.insert(pool.end(), e.tabs.begin(), e.tabs.end());
+  std::lock_guard<std::mutex> lk(g_range_mu);
+  if (g_range_cache.size() >= kRangeCache) {  // evict the least recently used
+    size_t old = 0;
+    for (size_t i = 1; i < g_range_cache.size(); ++i)
+      if (g_range_cache[i].used < g_range_cache[old].used) old = i;
+    g_range_cache.erase(g_range_cache.begin() + (long)old);
+  }
+  e.used = ++g_range_clock;
+  g_range_cache.push_back(std::move(e));
+  return NSFPS_OK;
+}
+
 // Build a job from `count` clouds with point counts n[i]; ranges resolved.
 int build_job(const uint64_t *n, uint64_t count, uint64_t k,
               const std::vector<nsfps_range> &ranges, const std::vector<uint32_t> &rid,
@@ -531,10 +580,9 @@ int build_job(const uint64_t *n, uint64_t count, uint64_t k,
   j.n = (uint32_t)tot;
   j.ranges.resize(ranges.size());
   for (size_t r = 0; r < ranges.size(); ++r) {
-    int rc = range_to_dev(ranges[r], &j.ranges[r], nullptr);
+    int rc = range_with_tables(ranges[r], j.ranges[r], j.tabs);
     if (rc) return rc;
     if (!j.ranges[r].direct) j.any_hashed = true;
-    cube_thresholds(j.ranges[r], j.tabs);
   }
   if (j.tabs.empty()) j.tabs.push_back(0.0f);
   j.rid = rid;
