@@ -223,6 +223,7 @@ struct DeviceCtx {
   cudaEvent_t ev[4] = {};
   bool ready = false;
   bool fixed = false;  // the workspace is the static scratch array: never (re)allocated
+  bool small_ready = false;  // small_setup_prepare ran on this device
   std::vector<SetupGraph> graphs;
   uint64_t graph_clock = 0;
   // host staging of a call's small uploads and downloads: pinned (one
@@ -269,6 +270,11 @@ void drop_setup_graphs(DeviceCtx *ctx) {
 // captures: instantiating a graph may allocate.
 cudaError_t run_setup_cached(DeviceCtx *ctx, const SetupArgs &sa, cudaStream_t st,
                              uint32_t &launches) {
+  if (sa.small_rounds && !ctx->small_ready) {
+    const cudaError_t e = small_setup_prepare();
+    if (e != cudaSuccess) return e;
+    ctx->small_ready = true;
+  }
   if (ctx->fixed) return run_setup(sa, st, launches);
   SetupGraph *hit = nullptr;
   for (SetupGraph &g : ctx->graphs)
@@ -599,6 +605,33 @@ int build_job(const uint64_t *n, uint64_t count, uint64_t k,
   return NSFPS_OK;
 }
 
+// The fused setup of small clouds (one CTA per cloud, two launches) when
+// every cloud has 1 .. kSmallCloudMax points, every range at most
+// kSmallMaxBuckets buckets, the candidate CTA counts sum to at most 512 and
+// the batch fills at most two waves of CTAs; its sort's register rounds, else
+// 0.
+// NSFPS_SMALL_SETUP=0 keeps the multi-launch pipeline.
+int small_setup(const Job &j, const uint32_t *cand, int ncand) {
+  static const bool off = [] {
+    const char *v = std::getenv("NSFPS_SMALL_SETUP");
+    return v && v[0] == '0';
+  }();
+  if (off || j.B == 0 || j.B > 296) return 0;
+  uint32_t mx = 0;
+  for (uint32_t c = 0; c < j.B; ++c) {
+    const uint32_t nc = j.poff[c + 1] - j.poff[c];
+    if (nc == 0) return 0;
+    mx = std::max(mx, nc);
+  }
+  if (mx > kSmallCloudMax) return 0;
+  for (const RangeDev &r : j.ranges)
+    if (r.total > kSmallMaxBuckets) return 0;
+  uint32_t sum = 0;  // the plan's per-CTA sums: at most 512 entries
+  for (int i = 0; i < ncand; ++i) sum += cand[i];
+  if (sum > 512u) return 0;
+  return small_setup_rounds(mx);
+}
+
 // Runs the whole pipeline for a job whose points are at d_xyz (device).
 // Writes B*k uint64 results to d_out and the B lengths to lens (host).
 int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_packed,
@@ -673,6 +706,7 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   sa.cand_host = cand;
   sa.ncand = ncand;
   sa.plan = b.plan;
+  sa.small_rounds = small_setup(j, cand, ncand);
   NSFPS_CUDA(run_setup_cached(ctx, sa, st, launches));
 
   // scalars, stats and plan come back as one copy (the staging buffer's

@@ -52,16 +52,32 @@ struct SetupArgs {
   uint32_t *leaf_start;       // n + 1
   float4 *leaf_lo, *leaf_hi;  // n each
   float *leaf_md;             // n
-  uint32_t *leaf_pre;         // n * (kMaxPreimages - 1) or null (direct ranges)
+  uint32_t *leaf_pre;         // n * kMaxPreimages or null (direct ranges)
   uint32_t *loff;             // B + 1 leaf offsets
   uint32_t *scalars;          // kScalarCount
   const uint32_t *cand;       // candidate CTA counts (device)
   const uint32_t *cand_host;  // same, host copy
   int ncand;
   uint32_t *plan;             // 3 * ncand (device)
+  // fused setup of small clouds (one CTA each, nsfps_setup.cu): register
+  // rounds of its sort (small_setup_rounds of the largest cloud), or 0 for the
+  // multi-launch pipeline.  Needs every cloud non-empty, every range's total
+  // buckets <= kSmallMaxBuckets and candidate CTA counts summing to <= 512.
+  int small_rounds;
 };
 
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches);
+
+// Largest cloud and bucket count of the fused setup of small clouds; its
+// sort's register rounds for a largest cloud of max_cloud points (0: too
+// large) and its dynamic shared memory.
+constexpr uint32_t kSmallCloudMax = 24576;
+constexpr uint32_t kSmallMaxBuckets = 1u << 17;
+int small_setup_rounds(uint32_t max_cloud);
+size_t small_setup_smem(int rounds);
+// Sets the fused setup's shared-memory opt-in on the current device; call
+// before run_setup (outside stream capture) when small_rounds is set.
+cudaError_t small_setup_prepare();
 
 // Tiles the radix sort splits n keys into.
 uint32_t radix_tiles(uint32_t n);

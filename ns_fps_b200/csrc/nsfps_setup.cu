@@ -155,6 +155,13 @@ void device_scan(const uint32_t *in, uint32_t *out, uint32_t n,
 // inputs, R = 4 (1024 keys) below kSmallSortKeys so that small sorts still
 // spread over the SMs.
 constexpr int kRsThreads = 256;
+// Fused setup of small clouds: threads per CTA, bits of the local point index
+// in a sort word.
+constexpr int kSmallThreads = 1024;
+constexpr int kSmallWarps = kSmallThreads / 32;
+// Largest sort rounds (words per lane) whose cloud is staged in shared memory.
+constexpr int kSmallStageRounds = 10;
+constexpr int kSmallIdxBits = 15;
 constexpr uint32_t kSmallSortKeys = 1u << 19;
 
 template <int R>
@@ -299,21 +306,14 @@ leaf_scatter(const uint32_t *__restrict__ run_start,
   }
 }
 
-__global__ void __launch_bounds__(256)
-leaf_meta(const uint32_t *__restrict__ keys, const float4 *__restrict__ pts,
-          const uint32_t *__restrict__ leaf_start,
-          const uint32_t *__restrict__ nleaves,
-          const uint32_t *__restrict__ poff, uint32_t B,
-          const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
-          const uint32_t *__restrict__ boff, float4 *__restrict__ leaf_lo,
-          float4 *__restrict__ leaf_hi, float *__restrict__ leaf_md,
-          uint32_t *__restrict__ leaf_pre) {
-  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
-  if (l >= *nleaves) return;
-  const uint32_t s = leaf_start[l], e = leaf_start[l + 1];
-  const uint32_t c = cloud_of(poff, B, s);
-  const RangeDev &r = ranges[rid[c]];
-  const uint32_t bucket = keys[s] - boff[c];
+// Leaf l = sorted points [s, e) of one bucket of range r: its bounding box,
+// the first maximum of d0 and the cell(s) whose cube membership selects it.
+__device__ __forceinline__ void build_leaf(uint32_t l, uint32_t s, uint32_t e, uint32_t bucket,
+                                           const RangeDev &r, const float4 *__restrict__ pts,
+                                           float4 *__restrict__ leaf_lo,
+                                           float4 *__restrict__ leaf_hi,
+                                           float *__restrict__ leaf_md,
+                                           uint32_t *__restrict__ leaf_pre) {
   float lx = FLT_MAX, ly = FLT_MAX, lz = FLT_MAX;
   float hx = -FLT_MAX, hy = -FLT_MAX, hz = -FLT_MAX;
   float md = -1.0f;
@@ -352,6 +352,23 @@ leaf_meta(const uint32_t *__restrict__ keys, const float4 *__restrict__ pts,
   leaf_lo[l] = make_float4(lx, ly, lz, __uint_as_float(cnt | (slot << 8) | (npre << 16)));
   leaf_hi[l] = make_float4(hx, hy, hz, __uint_as_float(cell0));
   leaf_md[l] = md;
+}
+
+__global__ void __launch_bounds__(256)
+leaf_meta(const uint32_t *__restrict__ keys, const float4 *__restrict__ pts,
+          const uint32_t *__restrict__ leaf_start,
+          const uint32_t *__restrict__ nleaves,
+          const uint32_t *__restrict__ poff, uint32_t B,
+          const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
+          const uint32_t *__restrict__ boff, float4 *__restrict__ leaf_lo,
+          float4 *__restrict__ leaf_hi, float *__restrict__ leaf_md,
+          uint32_t *__restrict__ leaf_pre) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= *nleaves) return;
+  const uint32_t s = leaf_start[l], e = leaf_start[l + 1];
+  const uint32_t c = cloud_of(poff, B, s);
+  build_leaf(l, s, e, keys[s] - boff[c], ranges[rid[c]], pts, leaf_lo, leaf_hi, leaf_md,
+             leaf_pre);
 }
 
 __global__ void cloud_leaf_offsets(const uint32_t *__restrict__ leafid,
@@ -403,6 +420,338 @@ __global__ void plan_partition(const float4 *__restrict__ leaf_lo,
       atomicMax(&plan[3 * i + 2], extra);
     }
   }
+}
+
+// ------------------------------------------------- small clouds, fused
+// Clouds of at most kSmallCloudMax points (24 x 1024): steps 1-5 with one
+// CTA of 1024 threads per cloud, in one launch for a single cloud and two
+// for a batch, instead of ~25.  The results are the pipeline's, bit for bit:
+// the sort is stable by bucket, so each cloud's sorted order, leaves and plan
+// entries are the same.
+
+// Lanes of `valid` whose digit equals this lane's (its low `bits` bits; the
+// rest are 0): one ballot per bit, a fixed cost whatever the digits
+// (__match_any_sync slows down with the number of distinct values).
+__device__ __forceinline__ uint32_t digit_peers(uint32_t d, int bits, uint32_t valid) {
+  uint32_t peers = valid;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    if (b >= bits) break;
+    const bool one = (d >> b) & 1u;
+    const uint32_t bal = __ballot_sync(kFull, one);
+    peers &= one ? bal : ~bal;
+  }
+  return peers;
+}
+
+// A range copied into shared memory by the CTA's first threads (word by word;
+// visible after the next barrier).
+__device__ __forceinline__ void load_range(RangeDev &dst, const RangeDev &src) {
+  static_assert(sizeof(RangeDev) % 4 == 0, "RangeDev is copied as words");
+  constexpr int kWords = (int)(sizeof(RangeDev) / 4);
+  if ((int)threadIdx.x < kWords)
+    reinterpret_cast<uint32_t *>(&dst)[threadIdx.x] =
+        reinterpret_cast<const uint32_t *>(&src)[threadIdx.x];
+}
+
+// Per-warp digit counts, warp-major with a padded row so that the lanes of a
+// warp touching different digits hit different banks.
+constexpr int kHistRow = 257;
+
+// Leaves and plan entries of cloud c, whose cnt leaves start at the sorted
+// positions lstart[s ..] with buckets lbucket[s ..] (s = poff[c]) and whose
+// leaf offset is L0: small_build_leaves runs build_leaf for each; small_plan,
+// for every candidate CTA count P, the largest point, leaf and
+// extra-preimage counts of the P CTAs the leaves are dealt to (leaf i of the
+// cloud to CTA i % P), merged into the plan with atomicMax as plan_partition
+// does.  All threads of the CTA call them; s_acc holds >= kSmallAcc words,
+// s_red >= 3 * ncand.
+constexpr int kSmallAcc = 2 * 512;
+__device__ __forceinline__ void small_build_leaves(
+    uint32_t c, uint32_t L0, uint32_t cnt, const RangeDev &r, const float4 *__restrict__ pts,
+    const uint32_t *__restrict__ poff, const uint32_t *__restrict__ lstart,
+    const uint32_t *__restrict__ lbucket, uint32_t *__restrict__ leaf_start,
+    float4 *__restrict__ leaf_lo, float4 *__restrict__ leaf_hi, float *__restrict__ leaf_md,
+    uint32_t *__restrict__ leaf_pre) {
+  const uint32_t s = poff[c], e = poff[c + 1];
+  for (uint32_t i = threadIdx.x; i < cnt; i += kSmallThreads) {
+    const uint32_t st = lstart[s + i], en = i + 1 < cnt ? lstart[s + i + 1] : e;
+    leaf_start[L0 + i] = st;
+    build_leaf(L0 + i, st, en, lbucket[s + i], r, pts, leaf_lo, leaf_hi, leaf_md, leaf_pre);
+  }
+}
+
+__device__ __forceinline__ void small_plan(uint32_t L0, uint32_t cnt,
+                                           const float4 *__restrict__ leaf_lo,
+                                           const uint32_t *__restrict__ cand, int ncand,
+                                           uint32_t *__restrict__ plan, uint32_t *s_acc,
+                                           uint32_t *s_red) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < kSmallAcc; i += kSmallThreads) s_acc[i] = 0u;
+  for (int i = tid; i < 3 * ncand; i += kSmallThreads) s_red[i] = 0u;
+  __syncthreads();  // the leaf writes before the call are visible to the whole CTA
+  // this thread's leaves i = tid + 1024 m: their points and extra preimages
+  uint32_t my_pts = 0, my_extra = 0;
+  for (uint32_t i = tid; i < cnt; i += kSmallThreads) {
+    const uint32_t w = __float_as_uint(leaf_lo[L0 + i].w);
+    const uint32_t npre = w >> 16;
+    my_pts += w & 0xffu;
+    my_extra += npre > 1 ? npre - 1 : 0u;
+  }
+  // per candidate, the sums of its CTAs at s_acc[2 (off + j) + {0, 1}]
+  const int lane = tid & 31;
+  uint32_t off = 0;
+  for (int ci = 0; ci < ncand; ++ci) {
+    const uint32_t P = cand[ci];
+    if ((kSmallThreads % P) == 0) {
+      // every leaf of this thread goes to CTA tid % P
+      uint32_t vp = my_pts, ve = my_extra;
+      if (P < 32) {  // fold the lanes of one residue within the warp first
+#pragma unroll
+        for (uint32_t o = 16; o >= 1; o >>= 1)
+          if (o >= P) {
+            vp += __shfl_xor_sync(kFull, vp, o);
+            ve += __shfl_xor_sync(kFull, ve, o);
+          }
+      }
+      if (P >= 32 || (uint32_t)lane < P) {
+        const uint32_t j = (uint32_t)tid % P;
+        if (vp) atomicAdd(&s_acc[2 * (off + j)], vp);
+        if (ve) atomicAdd(&s_acc[2 * (off + j) + 1], ve);
+      }
+    } else {
+      for (uint32_t i = tid; i < cnt; i += kSmallThreads) {
+        const uint32_t w = __float_as_uint(leaf_lo[L0 + i].w);
+        const uint32_t npre = w >> 16;
+        atomicAdd(&s_acc[2 * (off + i % P)], w & 0xffu);
+        if (npre > 1) atomicAdd(&s_acc[2 * (off + i % P) + 1], npre - 1);
+      }
+    }
+    off += P;
+  }
+  __syncthreads();
+  off = 0;
+  for (int ci = 0; ci < ncand; ++ci) {
+    const uint32_t P = cand[ci];
+    for (uint32_t j = tid; j < P; j += kSmallThreads) {
+      atomicMax(&s_red[3 * ci], s_acc[2 * (off + j)]);
+      atomicMax(&s_red[3 * ci + 1], cnt > j ? (cnt - j + P - 1) / P : 0u);
+      atomicMax(&s_red[3 * ci + 2], s_acc[2 * (off + j) + 1]);
+    }
+    off += P;
+  }
+  __syncthreads();
+  for (int i = tid; i < 3 * ncand; i += kSmallThreads) atomicMax(&plan[i], s_red[i]);
+}
+
+// small_sort: the cloud's points as words bucket << 15 | local index in
+// shared memory, sorted by an LSD radix sort over the bucket bits (8-bit
+// digits; warp w holds words [w R 32, (w+1) R 32) in registers in R ordered
+// rounds, so warp order, round order and lane order are the input order and
+// the scatter keeps it); then the sorted float4 points and permutation, and
+// the cloud's leaf starts, buckets and count (per-cloud scratch indexed from
+// the cloud's first point).  STAGE (clouds of at most 10 x 1024 points)
+// keeps the coordinates in shared memory for the gather.  A single cloud
+// (gridDim.x == 1) goes on to its leaves and plan in the same launch.
+template <int R>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+small_sort(const float *__restrict__ xyz, const uint32_t *__restrict__ poff,
+           const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
+           float4 *__restrict__ pts, uint32_t *__restrict__ perm,
+           uint32_t *__restrict__ lstart, uint32_t *__restrict__ lbucket,
+           uint32_t *__restrict__ lcount, uint32_t *__restrict__ leaf_start,
+           float4 *__restrict__ leaf_lo, float4 *__restrict__ leaf_hi,
+           float *__restrict__ leaf_md, uint32_t *__restrict__ leaf_pre,
+           uint32_t *__restrict__ loff, uint32_t *__restrict__ nleaves,
+           const uint32_t *__restrict__ cand, int ncand, uint32_t *__restrict__ plan) {
+  constexpr bool STAGE = R <= kSmallStageRounds;
+  extern __shared__ uint32_t small_sm[];
+  uint32_t *buf = small_sm;                                  // R * 1024 words
+  uint32_t *hist = small_sm + R * kSmallThreads;             // kSmallWarps x kHistRow
+  float *s_xyz = reinterpret_cast<float *>(hist + kSmallWarps * kHistRow);  // STAGE: 3 R 1024
+  __shared__ uint32_t s_warp[33];
+  __shared__ RangeDev s_range;
+  __shared__ uint32_t s_lut[3][1024];  // Morton spread of every axis index
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t c = blockIdx.x;
+  const uint32_t s = poff[c], nc = poff[c + 1] - s;
+  load_range(s_range, ranges[rid[c]]);
+  __syncthreads();
+  const RangeDev &r = s_range;
+  for (uint32_t a = 0; a < 3; ++a)
+    for (uint32_t v = tid; v < r.blocks[a]; v += kSmallThreads) s_lut[a][v] = spread_axis(r, (int)a, v);
+  if (STAGE)
+    for (uint32_t i = tid; i < 3 * nc; i += kSmallThreads) s_xyz[i] = xyz[3ull * s + i];
+  __syncthreads();
+  const uint32_t maxb = r.total - 1u;
+  const int kb = maxb ? 32 - __clz(maxb) : 0;  // bits of the largest bucket
+
+#pragma unroll 4
+  for (uint32_t i = tid; i < nc; i += kSmallThreads) {
+    uint32_t cx, cy, cz;
+    if (STAGE) {
+      cell_of(r, s_xyz[3 * i], s_xyz[3 * i + 1], s_xyz[3 * i + 2], cx, cy, cz);
+    } else {
+      const uint64_t q = 3ull * (s + i);
+      cell_of(r, xyz[q], xyz[q + 1], xyz[q + 2], cx, cy, cz);
+    }
+    const uint32_t code = s_lut[0][cx] | s_lut[1][cy] | s_lut[2][cz];  // bucket_of_cell
+    buf[i] = ((r.direct ? code : code % r.total) << kSmallIdxBits) | i;
+  }
+  __syncthreads();
+
+  const uint32_t lt = (1u << lane) - 1u;
+  const uint32_t wbase = (uint32_t)warp * (R * 32);
+  uint32_t *const hrow = hist + warp * kHistRow;
+  for (int shift = kSmallIdxBits; shift < kSmallIdxBits + kb; shift += 8) {
+    const int dbits = min(8, kSmallIdxBits + kb - shift);  // digit bits in use
+    uint32_t v[R];
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      const uint32_t idx = wbase + q * 32 + lane;
+      v[q] = idx < nc ? buf[idx] : 0u;
+    }
+    for (int i = tid; i < kSmallWarps * kHistRow; i += kSmallThreads) hist[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      const bool valid = wbase + q * 32 + lane < nc;
+      const uint32_t d = (v[q] >> shift) & 255u;
+      const uint32_t peers = digit_peers(d, dbits, __ballot_sync(kFull, valid));
+      if (valid && (peers & lt) == 0) hrow[d] += __popc(peers);
+      __syncwarp();
+    }
+    __syncthreads();
+    {  // (digit, warp) -> first output position: digits ascending, warps ascending
+      uint32_t tot = 0;
+      if (tid < 256)
+        for (int w = 0; w < kSmallWarps; ++w) tot += hist[w * kHistRow + tid];
+      uint32_t all;
+      uint32_t run = block_excl_scan<false>(tid < 256 ? tot : 0u, s_warp, all);
+      if (tid < 256)
+        for (int w = 0; w < kSmallWarps; ++w) {
+          const uint32_t cnt = hist[w * kHistRow + tid];
+          hist[w * kHistRow + tid] = run;
+          run += cnt;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      const bool valid = wbase + q * 32 + lane < nc;
+      const uint32_t d = (v[q] >> shift) & 255u;
+      const uint32_t peers = digit_peers(d, dbits, __ballot_sync(kFull, valid));
+      if (valid) buf[hrow[d] + __popc(peers & lt)] = v[q];
+      __syncwarp();
+      if (valid && (peers & lt) == 0) hrow[d] += __popc(peers);
+      __syncwarp();
+    }
+    __syncthreads();
+  }
+
+  // sorted points with d0 (the distance to the cloud's first point)
+  constexpr uint32_t kIdxMask = (1u << kSmallIdxBits) - 1u;
+  const float qx = nc ? xyz[3ull * s] : 0.0f, qy = nc ? xyz[3ull * s + 1] : 0.0f,
+              qz = nc ? xyz[3ull * s + 2] : 0.0f;
+  {
+#pragma unroll 4
+    for (uint32_t p = tid; p < nc; p += kSmallThreads) {
+      const uint32_t i = buf[p] & kIdxMask;
+      float x, y, z;
+      if (STAGE) {
+        x = s_xyz[3 * i]; y = s_xyz[3 * i + 1]; z = s_xyz[3 * i + 2];
+      } else {
+        const uint64_t q = 3ull * (s + i);
+        x = xyz[q]; y = xyz[q + 1]; z = xyz[q + 2];
+      }
+      const float d = sqdist(x, y, z, qx, qy, qz);
+      pts[s + p] = make_float4(x, y, z, (d < FLT_MAX) ? d : FLT_MAX);
+      perm[s + p] = s + i;
+    }
+  }
+
+  // leaves: runs of one bucket cut every kLeafSize points; thread t walks the
+  // sorted positions [t E, (t+1) E)
+  const uint32_t E = (nc + kSmallThreads - 1) / kSmallThreads;
+  const uint32_t p0 = min(nc, (uint32_t)tid * E), p1 = min(nc, p0 + E);
+  auto run_mark = [&](uint32_t p) {
+    return (p == 0 || (buf[p] >> kSmallIdxBits) != (buf[p - 1] >> kSmallIdxBits)) ? p : 0u;
+  };
+  uint32_t m = 0;
+  for (uint32_t p = p0; p < p1; ++p) m = max(m, run_mark(p));
+  uint32_t unused;
+  const uint32_t carry = block_excl_scan<true>(m, s_warp, unused);  // last run start before p0
+  uint32_t cur = carry, nl = 0;
+  for (uint32_t p = p0; p < p1; ++p) {
+    cur = max(cur, run_mark(p));
+    nl += ((p - cur) % kLeafSize) == 0 ? 1u : 0u;
+  }
+  uint32_t total;
+  uint32_t li = block_excl_scan<false>(nl, s_warp, total);
+  cur = carry;
+  for (uint32_t p = p0; p < p1; ++p) {
+    cur = max(cur, run_mark(p));
+    if (((p - cur) % kLeafSize) == 0) {
+      lstart[s + li] = s + p;
+      lbucket[s + li] = buf[p] >> kSmallIdxBits;
+      ++li;
+    }
+  }
+  if (gridDim.x > 1) {
+    if (tid == 0) lcount[c] = total;
+    return;
+  }
+  // one cloud: leaf offset 0, its leaves and the plan here
+  if (tid == 0) {
+    loff[0] = 0u;
+    loff[1] = total;
+    *nleaves = total;
+    leaf_start[total] = s + nc;
+  }
+  __syncthreads();  // lstart / lbucket / pts written above are visible to the CTA
+  small_build_leaves(c, 0u, total, r, pts, poff, lstart, lbucket, leaf_start, leaf_lo, leaf_hi,
+                     leaf_md, leaf_pre);
+  small_plan(0u, total, leaf_lo, cand, ncand, plan, hist, buf);
+}
+
+// small_leaves (batches): per cloud, its leaf offset (the leaves of the
+// clouds before it), then its leaves and plan entries.
+__global__ void __launch_bounds__(kSmallThreads, 1)
+small_leaves(const float4 *__restrict__ pts, const uint32_t *__restrict__ poff, uint32_t B,
+             const uint32_t *__restrict__ rid, const RangeDev *__restrict__ ranges,
+             const uint32_t *__restrict__ lstart, const uint32_t *__restrict__ lbucket,
+             const uint32_t *__restrict__ lcount, uint32_t *__restrict__ leaf_start,
+             float4 *__restrict__ leaf_lo, float4 *__restrict__ leaf_hi,
+             float *__restrict__ leaf_md, uint32_t *__restrict__ leaf_pre,
+             uint32_t *__restrict__ loff, uint32_t *__restrict__ nleaves,
+             const uint32_t *__restrict__ cand, int ncand, uint32_t *__restrict__ plan) {
+  __shared__ uint32_t s_warp[33];
+  __shared__ RangeDev s_range;
+  __shared__ uint32_t s_acc[kSmallAcc], s_red[3 * kMaxCand];
+  const int tid = threadIdx.x;
+  const uint32_t c = blockIdx.x;
+  load_range(s_range, ranges[rid[c]]);
+  uint32_t before = 0, all = 0;
+  for (uint32_t i = tid; i < B; i += kSmallThreads) {
+    const uint32_t v = lcount[i];
+    all += v;
+    before += i < c ? v : 0u;
+  }
+  uint32_t L0, L;
+  block_excl_scan<false>(before, s_warp, L0);  // (its barriers publish s_range)
+  block_excl_scan<false>(all, s_warp, L);
+  if (tid == 0) {
+    loff[c] = L0;
+    if (c + 1 == B) {
+      loff[B] = L;
+      *nleaves = L;
+      leaf_start[L] = poff[B];
+    }
+  }
+  const uint32_t cnt = lcount[c];
+  small_build_leaves(c, L0, cnt, s_range, pts, poff, lstart, lbucket, leaf_start, leaf_lo,
+                     leaf_hi, leaf_md, leaf_pre);
+  small_plan(L0, cnt, leaf_lo, cand, ncand, plan, s_acc, s_red);
 }
 
 // compute_bbox (src/yuezu_fps.cpp:648-670) of each cloud, on the device: the
@@ -504,6 +853,36 @@ cudaError_t run_cloud_bbox(const float *xyz, const uint32_t *poff, uint32_t B,
   return cudaGetLastError();
 }
 
+template <int R>
+cudaError_t small_sort_opt_in() {
+  return cudaFuncSetAttribute(small_sort<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)small_setup_smem(R));
+}
+
+cudaError_t small_setup_prepare() {
+  // the shared-memory opt-in of every instance, set outside stream capture
+  cudaError_t err;
+  if ((err = small_sort_opt_in<4>())) return err;
+  if ((err = small_sort_opt_in<8>())) return err;
+  if ((err = small_sort_opt_in<kSmallStageRounds>())) return err;
+  if ((err = small_sort_opt_in<16>())) return err;
+  return small_sort_opt_in<24>();
+}
+
+size_t small_setup_smem(int rounds) {
+  // sort words, digit counts, and the staged coordinates of clouds of at
+  // most kSmallStageRounds x 512 points
+  const size_t words = (size_t)rounds * kSmallThreads + kSmallWarps * kHistRow +
+                       (rounds <= kSmallStageRounds ? 3 * (size_t)rounds * kSmallThreads : 0);
+  return sizeof(uint32_t) * words;
+}
+
+int small_setup_rounds(uint32_t max_cloud) {
+  for (int r : {4, 8, kSmallStageRounds, 16, 24})
+    if (max_cloud <= (uint32_t)r * kSmallThreads) return r;
+  return 0;
+}
+
 uint32_t radix_tiles(uint32_t n) {
   return n < kSmallSortKeys ? cdiv(n, 8 * 4 * 32) : cdiv(n, 8 * 16 * 32);
 }
@@ -547,11 +926,43 @@ cudaError_t run_exclusive_scan(const uint32_t *in, uint32_t *out, uint32_t n,
   return cudaGetLastError();
 }
 
+template <int R>
+cudaError_t launch_small_sort(const SetupArgs &a, cudaStream_t st) {
+  small_sort<R><<<a.B, kSmallThreads, small_setup_smem(R), st>>>(
+      a.xyz, a.poff, a.rid, a.ranges, a.pts, a.perm, a.tmp0, a.tmp1, a.keys1, a.leaf_start,
+      a.leaf_lo, a.leaf_hi, a.leaf_md, a.leaf_pre, a.loff, a.scalars + kScalarLeaves, a.cand,
+      a.ncand, a.plan);
+  return cudaGetLastError();
+}
+
 cudaError_t run_setup(const SetupArgs &a, cudaStream_t st, uint32_t &launches) {
   const uint32_t n = a.n;
   const uint32_t B = a.B;
   cudaError_t err;
   if ((err = cudaMemsetAsync(a.scalars, 0, sizeof(uint32_t) * 8, st))) return err;
+
+  if (a.small_rounds) {  // every cloud fits one CTA: two launches
+    if ((err = cudaMemsetAsync(a.plan, 0, sizeof(uint32_t) * 3 * a.ncand, st))) return err;
+    switch (a.small_rounds) {
+      case 4: err = launch_small_sort<4>(a, st); break;
+      case 8: err = launch_small_sort<8>(a, st); break;
+      case kSmallStageRounds: err = launch_small_sort<kSmallStageRounds>(a, st); break;
+      case 16: err = launch_small_sort<16>(a, st); break;
+      case 24: err = launch_small_sort<24>(a, st); break;
+      default: return cudaErrorInvalidValue;
+    }
+    if (err) return err;
+    launches += 1;
+    if (B > 1) {  // the leaf offsets need every cloud's leaf count
+      small_leaves<<<B, kSmallThreads, 0, st>>>(a.pts, a.poff, B, a.rid, a.ranges, a.tmp0,
+                                                a.tmp1, a.keys1, a.leaf_start, a.leaf_lo,
+                                                a.leaf_hi, a.leaf_md, a.leaf_pre, a.loff,
+                                                a.scalars + kScalarLeaves, a.cand, a.ncand,
+                                                a.plan);
+      launches += 1;
+    }
+    return cudaGetLastError();
+  }
 
   bin_points<<<cdiv(n, 256), 256, 0, st>>>(a.xyz, n, a.poff, B, a.rid, a.ranges,
                                            a.boff, a.keys0, a.vals0);
