@@ -264,9 +264,11 @@ NSFPS_API int nsfps_group_points_device(const float *d_xyz, const uint64_t *poin
  * (summed over iterations), points actually re-evaluated after the exact
  * bounding-box skip, and the loop configuration (CTAs per cloud and mode:
  * 0 = per-step cluster loop, 2 = round-based cluster loop, 3 = round-based
- * loop over 64 or 128 co-resident CTAs for one cloud of at least 98,304
- * points or larger than a cluster's shared memory).  After a ball query (mode 4): setup = the grid build, loop = the
- * query kernel, launches = its kernel launches; the work counters are 0.
+ * loop over co-resident CTAs: 64 or 128 for a single cloud of at least 4,096
+ * points, groups of up to 16 for a batch when the device cannot hold a
+ * cluster per cloud).  After a ball query (mode 4): setup = the grid build,
+ * loop = the query kernel, launches = its kernel launches; the work counters
+ * are 0.
  * Enabled by nsfps_set_profiling. */
 typedef struct nsfps_profile {
   float setup_ms, loop_ms, total_ms;

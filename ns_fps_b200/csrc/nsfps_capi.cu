@@ -764,12 +764,11 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
     rounds = false;
     select();
   }
-  // one cloud too large for a cluster: the grid-wide round loop over P
-  // co-resident CTAs (one per SM), the smallest P that fits
   // A single cloud too large for a cluster takes the grid-wide round loop
   // over P co-resident CTAs (one per SM), the smallest P that fits.  So does
-  // a single cloud of many points that fits a cluster: over more CTAs its
-  // parts are smaller (lighter workers, shorter lists) and it runs faster.
+  // a single cloud of kGridMinPoints or more that fits a cluster: over more
+  // CTAs its parts are smaller (lighter workers, shorter lists) and each round
+  // replays more candidates, so it runs faster.
   bool grid = false;
   uint32_t groups = 1;
   if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&

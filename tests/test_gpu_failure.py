@@ -9,9 +9,10 @@ failure mode, so these pin this engine's own contract:
   a flag nothing else sets -- so every wait for it runs out; the call must
   return NSFPS_ERR_TIMEOUT, and the next call on the same device must return
   the oracle's samples (the context is still usable).  This runs each loop
-  variant: the grid-wide round loop (lists in global memory), the round loop
-  in one thread-block cluster and the per-step loop (both writing into other
-  CTAs' shared memory, so their exit must wait for every CTA);
+  variant: the grid-wide round loop (lists in global memory; a single
+  cloud), the round loop in thread-block clusters (a batch of two clouds,
+  one cluster each) and the per-step loop (both writing into other CTAs'
+  shared memory, so their exit must wait for every CTA);
 * a workspace request that fails returns NSFPS_ERR_OOM with a message, also
   from one worker thread of the multi-device sharder, and the next call
   succeeds;
@@ -51,7 +52,7 @@ def _cases():
     c2 = S.CONFIGS["c2"]
     scan = S.lidar_scan(seed=21)                       # 122,880 points: grid-wide loop
     c1 = S.CONFIGS["c1"]
-    gauss = S.make("c1", seed=5, count=1)[0]          # 10,000 points: one cluster
+    gauss = [S.gaussian_cloud(c1.n, 5), S.gaussian_cloud(c1.n, 6)]  # a cluster each
     rs = np.random.RandomState(9)
     hashed = (rs.rand(6000, 3) * [3, 5, 7]).astype(np.float32)
     return {
@@ -63,33 +64,42 @@ def _cases():
 
 @pytest.mark.parametrize("variant", ["grid", "cluster", "step"])
 def test_withheld_exchange_times_out_and_device_recovers(variant):
-    pts, k, bounds, blocks, mode, cta, step = _cases()[variant]
-    exp = oracle.fps(pts, k, bounds, blocks)
+    clouds, k, bounds, blocks, mode, cta, step = _cases()[variant]
+    if not isinstance(clouds, list):
+        clouds = [clouds]
+    exp = [oracle.fps(c, k, bounds, blocks) for c in clouds]
+    run = lambda: capi.fps_batched(clouds, k, bounds, blocks)
+
+    def check(got):
+        for g, e in zip(got, exp):
+            np.testing.assert_array_equal(g, e)
     # the layout under test is the one that runs
-    got, prof = _profiled(lambda: capi.fps(pts, k, bounds, blocks))
+    got, prof = _profiled(run)
     assert prof.mode == mode, f"expected loop mode {mode}, ran {prof.mode}"
     assert prof.ctas_per_cloud > cta
-    np.testing.assert_array_equal(got, exp)
+    check(got)
 
     capi.set_test_hooks(wait_limit_ns=WAIT_NS, withhold_cta=cta, withhold_step=step)
     with pytest.raises(RuntimeError, match=f"rc={capi.ERR_TIMEOUT}.*timed out"):
-        capi.fps(pts, k, bounds, blocks)
+        run()
     capi.set_test_hooks(reset=True)
     # the same device, the next call: exact samples again (twice)
     for _ in range(2):
-        np.testing.assert_array_equal(capi.fps(pts, k, bounds, blocks), exp)
+        check(run())
 
 
 def test_withhold_after_the_last_round_changes_nothing():
     """A hook aimed at a round the call never reaches leaves the call alone."""
-    pts, k, bounds, blocks, _, cta, _ = _cases()["cluster"]
+    clouds, k, bounds, blocks, _, cta, _ = _cases()["cluster"]
     capi.set_test_hooks(wait_limit_ns=WAIT_NS, withhold_cta=cta, withhold_step=1_000_000)
-    np.testing.assert_array_equal(capi.fps(pts, k, bounds, blocks),
-                                  oracle.fps(pts, k, bounds, blocks))
+    got = capi.fps_batched(clouds, k, bounds, blocks)
+    for g, c in zip(got, clouds):
+        np.testing.assert_array_equal(g, oracle.fps(c, k, bounds, blocks))
 
 
 def test_failed_workspace_request_returns_oom_then_recovers():
     pts, k, bounds, blocks, _, _, _ = _cases()["cluster"]
+    pts = pts[0]
     exp = oracle.fps(pts, k, bounds, blocks)
     capi.set_test_hooks(fail_alloc_device=0)
     with pytest.raises(RuntimeError, match=f"rc={capi.ERR_OOM}.*injected"):

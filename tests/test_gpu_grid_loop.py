@@ -1,7 +1,7 @@
 """GPU parity of the large-cloud layouts of the round loop against the CPU
 oracle: bit-exact indices.
 
-* The grid-wide loop (one cloud of at least 98,304 points over 64 or 128
+* The grid-wide loop (one cloud of at least 4,096 points over 64 or 128
   co-resident CTAs, 384 or 512 published candidates per round) on seeded
   random clouds: the golden vectors pin it on the c2 and c4 configs only;
   these cases add exact distance ties (quantised coordinates), clamped

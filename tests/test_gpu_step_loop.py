@@ -62,7 +62,7 @@ def test_step_loop_matches_round_loop(tmp_path):
     rounds = _run(tmp_path, clouds, spec, {}, "rounds")
     steps = _run(tmp_path, clouds, spec, {"NSFPS_STEP_LOOP": "1"}, "steps")
     for name, (k, bounds, blocks) in spec.items():
-        assert int(rounds[name + "_mode"][0]) == 2, name  # the round-based loop ran
+        assert int(rounds[name + "_mode"][0]) in (2, 3), name  # a round-based loop ran
         assert int(steps[name + "_mode"][0]) == 0, name   # the per-step loop ran
         np.testing.assert_array_equal(rounds[name], steps[name], err_msg=name)
         if name == "c1":

@@ -6,8 +6,9 @@ only when every axis has at most 64 of them; wider axes take the table walk in
 shared memory.  The reference's KITTI harness uses exactly such a grid: the
 bounding box +- 1e-6 with 128 x 128 x 2 blocks on frames filtered to z >= -5
 (eval/src_cpu/compare_cpu_test_kitti.cpp:202-245).  These tests run that path
-in both round loops -- the grid-wide loop (one cloud of at least 98,304
-points) and the loop in one cluster (~20k points) -- and check which ran:
+in both round loops -- the grid-wide loop (a single cloud) and the loop in
+thread-block clusters (a batch of ~20k-point clouds, one cluster each) -- and
+check which ran:
 
 * goldens made by the compiled reference (tests/golden: kitti_like_*,
   wide_*), including the path through the .bin reader straight into device
@@ -51,19 +52,43 @@ def _points(name):
     return CASES[name].points()
 
 
-@pytest.mark.parametrize("name,mode", [("kitti_like_f0_128x128x2", MODE_GRID),
-                                       ("kitti_like_f1_sub6_128x128x2", MODE_ROUNDS),
-                                       ("wide_1024x2x2", MODE_ROUNDS),
-                                       ("wide_2x256x4_100k", MODE_GRID)])
-def test_wide_axis_goldens_run_the_round_loops(name, mode):
+@pytest.mark.parametrize("name", ["kitti_like_f0_128x128x2", "kitti_like_f1_sub6_128x128x2",
+                                  "wide_1024x2x2", "wide_2x256x4_100k"])
+def test_wide_axis_goldens_run_the_round_loops(name):
     case = CASES[name]
     pts = _points(name)
     got, prof = _profiled(lambda: capi.fps(pts, case.k, case.bounds, case.blocks))
-    assert prof.mode == mode, f"{name}: expected loop mode {mode}, ran {prof.mode}"
+    assert prof.mode == MODE_GRID, f"{name}: expected the grid-wide loop, ran {prof.mode}"
     assert max(case.blocks) > 64
     exp = GOLD_NPZ[name + "/indices"].astype(np.uint64)
     assert GOLD[name]["stored"] == "full" and len(got) == GOLD[name]["len"]
     np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("name", ["kitti_like_f1_sub6_128x128x2", "wide_1024x2x2"])
+def test_wide_axis_goldens_in_clusters(name):
+    """The same golden cloud twice in one device batch: a cluster per cloud
+    (each cloud's bounding box reduced on the device when the case has none)."""
+    import torch
+    case = CASES[name]
+    pts = _points(name)
+    n = pts.shape[0]
+    d = torch.from_numpy(np.concatenate([pts, pts])).cuda()
+    out = torch.empty(2 * case.k, dtype=torch.int64, device="cuda")
+    offs = np.array([0, n, 2 * n], np.int64)
+    if case.bounds is None:
+        run = lambda: capi.fps_device_with_bbox(d.data_ptr(), offs, case.k, case.blocks,
+                                                out.data_ptr())
+    else:
+        run = lambda: capi.fps_device(d.data_ptr(), offs, case.k, (case.bounds, case.blocks),
+                                      False, out.data_ptr())
+    lens, prof = _profiled(run)
+    assert prof.mode == MODE_ROUNDS, f"{name}: expected the cluster loop, ran {prof.mode}"
+    exp = GOLD_NPZ[name + "/indices"].astype(np.uint64)
+    got = out.cpu().numpy().astype(np.uint64).reshape(2, case.k)
+    for c in range(2):
+        assert lens[c] == len(exp)
+        np.testing.assert_array_equal(got[c][:len(exp)], exp)
 
 
 def test_kitti_bin_straight_to_device_matches_reference_golden(tmp_path):
@@ -99,14 +124,18 @@ def _wide_cloud(rs, n, kind):
 
 
 @pytest.mark.parametrize("blocks", [(128, 4, 2), (8, 256, 4), (2, 2, 1024)])
-@pytest.mark.parametrize("n,mode", [(20_000, MODE_ROUNDS), (110_000, MODE_GRID)])
-def test_wide_axis_seeded_grids_match_oracle(blocks, n, mode):
+@pytest.mark.parametrize("n,batch", [(20_000, 1), (20_000, 2), (110_000, 1)])
+def test_wide_axis_seeded_grids_match_oracle(blocks, n, batch):
+    """One cloud: the grid-wide loop; two ~20k-point clouds: a cluster each."""
     rs = np.random.RandomState(sum(blocks) + n)
-    pts = _wide_cloud(rs, n, (blocks.index(max(blocks)) + n // 10000) % 2)
-    lo, hi = pts.min(0) - 1e-3, pts.max(0) + 1e-3
+    clouds = [_wide_cloud(rs, n, (blocks.index(max(blocks)) + n // 10000 + i) % 2)
+              for i in range(batch)]
+    allp = np.concatenate(clouds)
+    lo, hi = allp.min(0) - 1e-3, allp.max(0) + 1e-3
     bounds = (lo[0], hi[0], lo[1], hi[1], lo[2], hi[2])
     k = 2500
-    exp = oracle.fps(pts, k, bounds, blocks)
-    got, prof = _profiled(lambda: capi.fps(pts, k, bounds, blocks))
+    got, prof = _profiled(lambda: capi.fps_batched(clouds, k, bounds, blocks))
+    mode = MODE_GRID if batch == 1 else MODE_ROUNDS
     assert prof.mode == mode, f"expected loop mode {mode}, ran {prof.mode}"
-    np.testing.assert_array_equal(got, exp)
+    for g, c in zip(got, clouds):
+        np.testing.assert_array_equal(g, oracle.fps(c, k, bounds, blocks))
