@@ -407,6 +407,9 @@ constexpr int kNumCluster = 5;
 constexpr uint32_t kMaxGridP = 128;
 // CTAs a grid-wide launch may hold (list buffers and counters are sized for it)
 constexpr uint32_t kMaxGridCtas = 256;
+// CTAs of the grid-wide loop of a small single cloud launched without a plan
+// round trip (run_job)
+constexpr uint32_t kDirectP = 64;
 // Points from which one cloud runs on the grid-wide loop even when it fits a
 // cluster.
 constexpr uint32_t kGridMinPoints = NSFPS_GRID_MIN_POINTS;
@@ -709,15 +712,44 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   sa.small_rounds = small_setup(j, cand, ncand);
   NSFPS_CUDA(run_setup_cached(ctx, sa, st, launches));
 
-  // scalars, stats and plan come back as one copy (the staging buffer's
-  // upload was issued before on the same stream, so it has been read)
   uint32_t hplan[3 * kMaxCand] = {};
   uint32_t hscal[kScalarCount] = {};
-  NSFPS_CUDA(cudaMemcpyAsync(hs, b.ctrl, kCtrlCount, cudaMemcpyDeviceToHost, st));
-  if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
-  NSFPS_CUDA(cudaStreamSynchronize(st));
-  std::memcpy(hscal, hs + kCtrlScalars, sizeof(hscal));
-  std::memcpy(hplan, hs + kCtrlPlan, sizeof(uint32_t) * 3 * ncand);
+  uint32_t max_tab = 0;
+  for (const RangeDev &r : j.ranges)
+    if (r.fast_cube)
+      max_tab = std::max(max_tab, r.blocks[0] + r.blocks[1] + r.blocks[2] - 3);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+  // A single small cloud whose worst case -- every leaf a single point --
+  // still gives each worker thread at most one leaf of a 64-CTA grid (and
+  // fits shared memory) is launched right behind its setup with that worst
+  // case as its plan: the layout is the one the data would get, and the call
+  // makes no round trip to the host for the plan.
+  int direct = -1;
+  if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&
+      j.n >= kGridMinPoints && (uint32_t)sms >= kDirectP &&
+      rounds_grid_candidates_per_cta(kDirectP) > 0) {
+    const uint32_t lmax = (j.n + kDirectP - 1) / kDirectP;
+    const uint32_t pmax = std::min<uint32_t>(j.n, (uint32_t)kLeafSize * lmax);
+    for (int i = 0; i < ncand; ++i)
+      if (cand[i] == kDirectP && rounds_leaves_per_thread(lmax) == 1 && pmax <= 65535 &&
+          rounds_smem_bytes(pmax, lmax, max_tab) <= (size_t)rounds_max_smem(kDirectP)) {
+        direct = i;
+        hplan[3 * i] = pmax;
+        hplan[3 * i + 1] = lmax;
+      }
+  }
+  if (direct < 0) {
+    // scalars, stats and plan come back as one copy (the staging buffer's
+    // upload was issued before on the same stream, so it has been read)
+    NSFPS_CUDA(cudaMemcpyAsync(hs, b.ctrl, kCtrlCount, cudaMemcpyDeviceToHost, st));
+    if (prof) NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
+    NSFPS_CUDA(cudaStreamSynchronize(st));
+    std::memcpy(hscal, hs + kCtrlScalars, sizeof(hscal));
+    std::memcpy(hplan, hs + kCtrlPlan, sizeof(uint32_t) * 3 * ncand);
+  } else if (prof) {
+    NSFPS_CUDA(cudaEventRecord(ctx->ev[1], st));
+  }
 
   // CTAs per cloud: the smallest count whose largest part fits in shared
   // memory; then, while every cloud still gets its own SMs, keep doubling it:
@@ -725,12 +757,6 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   // the same steps), for the per-step loop until each thread owns a single
   // leaf (more CTAs also mean more proposals per step there).
   const int max_smem = loop_max_smem();
-  uint32_t max_tab = 0;
-  for (const RangeDev &r : j.ranges)
-    if (r.fast_cube)
-      max_tab = std::max(max_tab, r.blocks[0] + r.blocks[1] + r.blocks[2] - 3);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
   // direct ranges use the round-based loop, hashed ranges the per-step one;
   // so do parts with more leaves than the round-based loop's threads can own
   bool rounds = !j.any_hashed && !g_force_steps.load();
@@ -759,63 +785,71 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
       pi = i; m_sel = m; bytes_sel = bytes;
     }
   };
-  select();
-  if (pi < 0 && rounds) {
-    rounds = false;
-    select();
-  }
-  // A single cloud too large for a cluster takes the grid-wide round loop
-  // over P co-resident CTAs (one per SM), the smallest P that fits.  So does
-  // a single cloud of kGridMinPoints or more that fits a cluster: over more
-  // CTAs its parts are smaller (lighter workers, shorter lists) and each round
-  // replays more candidates, so it runs faster.
   bool grid = false;
   uint32_t groups = 1;
-  if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&
-      (pi < 0 || j.n >= kGridMinPoints)) {
-    for (int i = kNumCluster; i < kNumSingle && !grid; ++i) {
-      const uint32_t P = cand[i];
-      // one cloud: 64 or 128 CTAs (32 with 8 candidates each was slower on
-      // c2, 4.89 against 4.16 ms at 64)
-      if (P > (uint32_t)sms || P > kMaxGridP || (P != 64u && P != 128u)) continue;
-      const bool was_rounds = rounds;
-      rounds = true;
-      int m;
-      size_t bytes;
-      if (fits(i, m, bytes)) {
-        pi = i; m_sel = m; bytes_sel = bytes; grid = true;
-      } else {
-        rounds = was_rounds;
+  if (direct >= 0) {
+    pi = direct;
+    m_sel = 1;
+    bytes_sel = rounds_smem_bytes(hplan[3 * direct], hplan[3 * direct + 1], max_tab);
+    grid = true;
+  } else {
+    select();
+    if (pi < 0 && rounds) {
+      rounds = false;
+      select();
+    }
+    // A single cloud too large for a cluster takes the grid-wide round loop
+    // over P co-resident CTAs (one per SM), the smallest P that fits.  So does
+    // a single cloud of kGridMinPoints or more that fits a cluster: over more
+    // CTAs its parts are smaller (lighter workers, shorter lists) and each round
+    // replays more candidates, so it runs faster.
+    if (j.B == 1 && !j.any_hashed && !g_force_steps.load() && b.glist &&
+        (pi < 0 || j.n >= kGridMinPoints)) {
+      for (int i = kNumCluster; i < kNumSingle && !grid; ++i) {
+        const uint32_t P = cand[i];
+        // one cloud: 64 or 128 CTAs (32 with 8 candidates each was slower on
+        // c2, 4.89 against 4.16 ms at 64)
+        if (P > (uint32_t)sms || P > kMaxGridP || (P != 64u && P != 128u)) continue;
+        const bool was_rounds = rounds;
+        rounds = true;
+        int m;
+        size_t bytes;
+        if (fits(i, m, bytes)) {
+          pi = i; m_sel = m; bytes_sel = bytes; grid = true;
+        } else {
+          rounds = was_rounds;
+        }
       }
     }
-  }
-  // A batch whose clouds fit the round loop: the layout that keeps the most
-  // clouds running at once.  A cluster must fit one GPC, so at one CTA per
-  // SM the device holds only some clusters (7 of 16 CTAs on B200, 112 of
-  // 148 SMs); groups of co-resident CTAs (the grid-wide loop, one group per
-  // cloud in turn) have no such limit.
-  if (j.B > 1 && rounds && pi >= 0 && !g_force_steps.load()) {
-    const uint32_t Pc = cand[pi];
-    int force = -1;  // NSFPS_BATCH_GROUP_CTAS: 0 = clusters, P = groups of P CTAs
-    if (const char *v = std::getenv("NSFPS_BATCH_GROUP_CTAS")) force = std::atoi(v);
-    const int cap = force < 0 ? rounds_cluster_capacity(Pc, m_sel, std::max<size_t>(bytes_sel, 16)) : 0;
-    const uint32_t conc_c = cap > 0 ? std::min<uint32_t>(j.B, (uint32_t)cap * 1u) : j.B;
-    int gi = -1;
-    if (force > 0) {
-      for (int i = 0; i < kNumBatch; ++i)
-        if (cand[i] == (uint32_t)force) gi = i;
-    } else if (force < 0 && conc_c < j.B && Pc >= 2) {
-      gi = pi;  // the same CTAs per cloud, more clouds at once
-    }
-    if (gi >= 0) {
-      int m;
-      size_t bytes;
-      const uint32_t P = cand[gi];
-      if (P <= (uint32_t)sms && rounds_grid_candidates_per_cta(P) > 0 && fits(gi, m, bytes)) {
-        pi = gi; m_sel = m; bytes_sel = bytes; grid = true;
-        groups = std::min<uint32_t>(j.B, std::min<uint32_t>((uint32_t)sms, kMaxGridCtas) / P);
-      } else if (force > 0) {
-        return set_error(NSFPS_ERR_UNSUPPORTED, "NSFPS_BATCH_GROUP_CTAS=%d does not fit", force);
+    // A batch whose clouds fit the round loop: the layout that keeps the most
+    // clouds running at once.  A cluster must fit one GPC, so at one CTA per
+    // SM the device holds only some clusters (7 of 16 CTAs on B200, 112 of
+    // 148 SMs); groups of co-resident CTAs (the grid-wide loop, one group per
+    // cloud in turn) have no such limit.
+    if (j.B > 1 && rounds && pi >= 0 && !g_force_steps.load()) {
+      const uint32_t Pc = cand[pi];
+      int force = -1;  // NSFPS_BATCH_GROUP_CTAS: 0 = clusters, P = groups of P CTAs
+      if (const char *v = std::getenv("NSFPS_BATCH_GROUP_CTAS")) force = std::atoi(v);
+      const int cap =
+          force < 0 ? rounds_cluster_capacity(Pc, m_sel, std::max<size_t>(bytes_sel, 16)) : 0;
+      const uint32_t conc_c = cap > 0 ? std::min<uint32_t>(j.B, (uint32_t)cap * 1u) : j.B;
+      int gi = -1;
+      if (force > 0) {
+        for (int i = 0; i < kNumBatch; ++i)
+          if (cand[i] == (uint32_t)force) gi = i;
+      } else if (force < 0 && conc_c < j.B && Pc >= 2) {
+        gi = pi;  // the same CTAs per cloud, more clouds at once
+      }
+      if (gi >= 0) {
+        int m;
+        size_t bytes;
+        const uint32_t P = cand[gi];
+        if (P <= (uint32_t)sms && rounds_grid_candidates_per_cta(P) > 0 && fits(gi, m, bytes)) {
+          pi = gi; m_sel = m; bytes_sel = bytes; grid = true;
+          groups = std::min<uint32_t>(j.B, std::min<uint32_t>((uint32_t)sms, kMaxGridCtas) / P);
+        } else if (force > 0) {
+          return set_error(NSFPS_ERR_UNSUPPORTED, "NSFPS_BATCH_GROUP_CTAS=%d does not fit", force);
+        }
       }
     }
   }
