@@ -684,34 +684,6 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   NSFPS_CUDA(cudaMemcpyAsync(b.params, hs, L.bytes, cudaMemcpyHostToDevice, st));
   NSFPS_CUDA(cudaMemsetAsync(b.stats, 0, 4 * sizeof(unsigned long long), st));
 
-  SetupArgs sa;
-  std::memset(&sa, 0, sizeof(sa));  // compared bytewise by the graph cache
-  sa.n = j.n;
-  sa.B = j.B;
-  sa.max_key = (uint32_t)(j.total_buckets - 1);
-  sa.xyz = d_xyz;
-  sa.poff = b.poff;
-  sa.rid = b.rid;
-  sa.ranges = b.ranges;
-  sa.boff = b.boff;
-  sa.keys0 = b.keys0; sa.vals0 = b.vals0; sa.keys1 = b.keys1; sa.vals1 = b.vals1;
-  sa.hist = b.hist;
-  sa.partial = b.partial;
-  sa.pts = b.pts;
-  sa.perm = b.perm;
-  sa.tmp0 = b.tmp0; sa.tmp1 = b.tmp1;
-  sa.leaf_start = b.leaf_start;
-  sa.leaf_lo = b.leaf_lo; sa.leaf_hi = b.leaf_hi; sa.leaf_md = b.leaf_md;
-  sa.leaf_pre = b.leaf_pre;
-  sa.loff = b.loff;
-  sa.scalars = b.scalars;
-  sa.cand = b.cand;
-  sa.cand_host = cand;
-  sa.ncand = ncand;
-  sa.plan = b.plan;
-  sa.small_rounds = small_setup(j, cand, ncand);
-  NSFPS_CUDA(run_setup_cached(ctx, sa, st, launches));
-
   uint32_t hplan[3 * kMaxCand] = {};
   uint32_t hscal[kScalarCount] = {};
   uint32_t max_tab = 0;
@@ -739,6 +711,34 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
         hplan[3 * i + 1] = lmax;
       }
   }
+  SetupArgs sa;
+  std::memset(&sa, 0, sizeof(sa));  // compared bytewise by the graph cache
+  sa.n = j.n;
+  sa.B = j.B;
+  sa.max_key = (uint32_t)(j.total_buckets - 1);
+  sa.xyz = d_xyz;
+  sa.poff = b.poff;
+  sa.rid = b.rid;
+  sa.ranges = b.ranges;
+  sa.boff = b.boff;
+  sa.keys0 = b.keys0; sa.vals0 = b.vals0; sa.keys1 = b.keys1; sa.vals1 = b.vals1;
+  sa.hist = b.hist;
+  sa.partial = b.partial;
+  sa.pts = b.pts;
+  sa.perm = b.perm;
+  sa.tmp0 = b.tmp0; sa.tmp1 = b.tmp1;
+  sa.leaf_start = b.leaf_start;
+  sa.leaf_lo = b.leaf_lo; sa.leaf_hi = b.leaf_hi; sa.leaf_md = b.leaf_md;
+  sa.leaf_pre = b.leaf_pre;
+  sa.loff = b.loff;
+  sa.scalars = b.scalars;
+  sa.cand = b.cand;
+  sa.cand_host = cand;
+  sa.ncand = direct >= 0 ? 0 : ncand;  // a direct launch reads no plan
+  sa.plan = b.plan;
+  sa.small_rounds = small_setup(j, cand, ncand);
+  NSFPS_CUDA(run_setup_cached(ctx, sa, st, launches));
+
   if (direct < 0) {
     // scalars, stats and plan come back as one copy (the staging buffer's
     // upload was issued before on the same stream, so it has been read)

@@ -487,6 +487,7 @@ __device__ __forceinline__ void small_plan(uint32_t L0, uint32_t cnt,
                                            uint32_t *__restrict__ plan, uint32_t *s_acc,
                                            uint32_t *s_red) {
   const int tid = threadIdx.x;
+  if (ncand == 0) return;  // (uniform over the CTA)
   for (int i = tid; i < kSmallAcc; i += kSmallThreads) s_acc[i] = 0u;
   for (int i = tid; i < 3 * ncand; i += kSmallThreads) s_red[i] = 0u;
   __syncthreads();  // the leaf writes before the call are visible to the whole CTA
