@@ -483,7 +483,7 @@ size_t carve(Carver &c, const Job &j, bool own_xyz, bool own_out, Buffers &b) {
   // at most 16 CTAs over at most kMaxGridCtas
   const size_t glist_bytes =
       j.B == 1 ? std::max(rounds_grid_list_bytes(64, 1), rounds_grid_list_bytes(128, 1))
-               : rounds_grid_list_bytes(16, kMaxGridCtas / 16);
+               : rounds_group_list_bytes(kMaxGridCtas);
   b.glist = c.take<uint4>(glist_bytes / 16);
   b.gbar = c.take<uint32_t>(kMaxGridCtas);
   return align_up(c.off, 256);

@@ -146,9 +146,10 @@ struct LoopPlan {
 // per CTA, or 0 when none does.
 int loop_leaves_per_thread(uint32_t leaves);
 
-// The round-based loop (direct ranges only): candidates per CTA, shared
+// The round-based loop (direct ranges only): candidates per CTA of a part of
+// a cloud over P <= 16 CTAs holding up to `pts` points per CTA, shared
 // memory, launch.
-int rounds_candidates_per_cta(uint32_t P);
+int rounds_candidates_per_cta(uint32_t P, uint32_t pts);
 int rounds_leaves_per_thread(uint32_t leaves);
 size_t rounds_smem_bytes(uint32_t pts, uint32_t leaves, uint32_t tab);
 int rounds_max_smem(uint32_t P);
@@ -161,6 +162,9 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
 // (for the choice between the two layouts; 0 when unknown).
 int rounds_grid_candidates_per_cta(uint32_t P);
 size_t rounds_grid_list_bytes(uint32_t P, uint32_t groups);
+// Bytes of the global list buffers of batch groups over `ctas` CTAs in all,
+// whatever their size.
+size_t rounds_group_list_bytes(uint32_t ctas);
 int rounds_cluster_capacity(uint32_t P, int m, size_t smem);
 
 cudaError_t run_loop(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,

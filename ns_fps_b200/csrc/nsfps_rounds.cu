@@ -78,11 +78,33 @@ __device__ __forceinline__ int worker_index(int warp) {
   if (kIdle && warp >= 4 && warp < 4 + kIdle) return -1;
   return warp - kReplay - ((kIdle && warp >= 4 + kIdle) ? kIdle : 0);
 }
-// Candidates each CTA of a cluster publishes per round (a build-time choice).
+// Candidates each CTA of a cluster or a batch group publishes per round
+// (build-time choices): NSFPS_ROUND_T for parts of fewer than
+// kBigPartPoints points per CTA; for larger parts NSFPS_ROUND_T_FEW when a
+// cloud has at most 4 CTAs, NSFPS_ROUND_T_BIG when it has more.  Few
+// candidates end a round early; many make every step and list dearer.  On
+// B200, 8 / 12 / 16 per CTA gave a batch of 32 clouds of 16,384 points at 4
+// CTAs each 3.373 / 3.252 / 3.225 ms per loop and 72 scans in groups of 16
+// CTAs 54.05 / 51.91 / 53.14 ms, while parts of 600 to 1,250 points per CTA
+// ran 1.5 to 4.6 % slower at 12 or 16 than at 8.
 #ifndef NSFPS_ROUND_T
 #define NSFPS_ROUND_T 8
 #endif
+#ifndef NSFPS_ROUND_T_BIG
+#define NSFPS_ROUND_T_BIG 12
+#endif
+#ifndef NSFPS_ROUND_T_FEW
+#define NSFPS_ROUND_T_FEW 16
+#endif
 constexpr int kRoundT = NSFPS_ROUND_T;
+constexpr int kRoundTBig = NSFPS_ROUND_T_BIG;
+constexpr int kRoundTFew = NSFPS_ROUND_T_FEW;
+constexpr uint32_t kBigPartPoints = 2048;
+// candidates per CTA of a large part of a cloud over P <= 16 CTAs
+__host__ __device__ constexpr int big_t(uint32_t P) { return P <= 4u ? kRoundTFew : kRoundTBig; }
+constexpr int kMaxPartT = (kRoundT > kRoundTBig ? kRoundT : kRoundTBig) > kRoundTFew
+                              ? (kRoundT > kRoundTBig ? kRoundT : kRoundTBig)
+                              : kRoundTFew;
 // Candidates per round, at most (P * T): the kernel's template parameter CAP,
 // 256 in a cluster and in the 64-CTA grid, 512 in the 128-CTA grid.
 constexpr int kClusterCap = kRoundT * 16 > 256 ? kRoundT * 16 : 256;
@@ -1220,16 +1242,21 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
 // the largest CTA bound; more candidates per CTA lower that bound but cost
 // every step more work: on c2 (P = 64) 4, 6 and 8 per CTA gave 4.160, 4.149
 // and 4.19 ms, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
-// Groups of at most 32 CTAs (batches) publish kRoundT each, as a cluster does.
+// Groups of at most 16 CTAs (batches) publish as a cluster does (at most
+// big_t(P) each).
 constexpr int grid_t(uint32_t P) {
-  return P == 64u ? 6 : (P == 128u ? 4 : (P <= 32u ? kRoundT : 0));
+  return P == 64u ? 6 : (P == 128u ? 4 : (P <= 16u ? big_t(P) : 0));
 }
 constexpr int grid_cap(uint32_t P) { return P == 64u || P == 128u ? (int)P * grid_t(P) : kClusterCap; }
-static_assert(32 * kRoundT <= kClusterCap, "groups of up to 32 CTAs fit the cluster capacity");
+static_assert(16 * kRoundT <= kClusterCap && 16 * kRoundTBig <= kClusterCap &&
+                  4 * kRoundTFew <= kClusterCap,
+              "parts of up to 16 CTAs fit the cluster capacity");
 
 }  // namespace
 
-int rounds_candidates_per_cta(uint32_t) { return kRoundT; }
+int rounds_candidates_per_cta(uint32_t P, uint32_t pts) {
+  return pts >= kBigPartPoints ? big_t(P) : kRoundT;
+}
 
 int rounds_leaves_per_thread(uint32_t leaves) {
   static const int ms[] = {1, 2, 3, 4, 6, 8};
@@ -1251,7 +1278,7 @@ int rounds_max_smem(uint32_t P) {
   // the grid-wide loop (P > one cluster) keeps smaller lists in shared memory
   const int ctl = P == 64u    ? (int)sizeof(RoundCtl<grid_t(64), grid_cap(64)>)
                   : P == 128u ? (int)sizeof(RoundCtl<grid_t(128), grid_cap(128)>)
-                              : (int)sizeof(RoundCtl<kRoundT, kClusterCap>);
+                              : (int)sizeof(RoundCtl<kMaxPartT, kClusterCap>);
   return optin - ctl - 1024;
 }
 
@@ -1262,24 +1289,34 @@ int rounds_grid_candidates_per_cta(uint32_t P) {
 size_t rounds_grid_list_bytes(uint32_t P, uint32_t groups) {
   const size_t list = P == 64u    ? sizeof(CtaList<grid_t(64)>)
                       : P == 128u ? sizeof(CtaList<grid_t(128)>)
-                                  : sizeof(CtaList<kRoundT>);
+                                  : sizeof(CtaList<kMaxPartT>);
   return grid_t(P) ? (size_t)groups * 2 * P * list : 0;
+}
+
+size_t rounds_group_list_bytes(uint32_t ctas) {
+  return (size_t)2 * ctas * sizeof(CtaList<kMaxPartT>);
+}
+
+template <int T>
+const void *cluster_kernel(int m) {
+  switch (m) {
+    case 1: return (const void *)fps_rounds_cluster<1, T, false, kClusterCap>;
+    case 2: return (const void *)fps_rounds_cluster<2, T, false, kClusterCap>;
+    case 3: return (const void *)fps_rounds_cluster<3, T, false, kClusterCap>;
+    case 4: return (const void *)fps_rounds_cluster<4, T, false, kClusterCap>;
+    case 6: return (const void *)fps_rounds_cluster<6, T, false, kClusterCap>;
+    case 8: return (const void *)fps_rounds_cluster<8, T, false, kClusterCap>;
+    default: return nullptr;
+  }
 }
 
 int rounds_cluster_capacity(uint32_t P, int m, size_t smem) {
   // clusters of P CTAs of the round kernel the device holds at once (a
   // cluster must fit one GPC: on B200 7 clusters of 16 CTAs at one CTA per SM)
   if (P == 0 || P > (uint32_t)kMaxClusterP) return 0;
-  const void *kern = nullptr;
-  switch (m) {
-    case 1: kern = (const void *)fps_rounds_cluster<1, kRoundT, false, kClusterCap>; break;
-    case 2: kern = (const void *)fps_rounds_cluster<2, kRoundT, false, kClusterCap>; break;
-    case 3: kern = (const void *)fps_rounds_cluster<3, kRoundT, false, kClusterCap>; break;
-    case 4: kern = (const void *)fps_rounds_cluster<4, kRoundT, false, kClusterCap>; break;
-    case 6: kern = (const void *)fps_rounds_cluster<6, kRoundT, false, kClusterCap>; break;
-    case 8: kern = (const void *)fps_rounds_cluster<8, kRoundT, false, kClusterCap>; break;
-    default: return 0;
-  }
+  // (the instance of the larger lists: its static shared memory bounds the others)
+  const void *kern = P <= 4u ? cluster_kernel<kRoundTFew>(m) : cluster_kernel<kRoundTBig>(m);
+  if (!kern) return 0;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
       (P > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1))) {
     cudaGetLastError();
@@ -1316,13 +1353,20 @@ cudaError_t run_rounds(const LoopArgs &a, const LoopPlan &plan, cudaStream_t st,
       err = a.P == 64u ? launch_rounds_m<grid_t(64), true, grid_cap(64)>(a, m, plan.smem_bytes, st)
                        : launch_rounds_m<grid_t(128), true, grid_cap(128)>(a, m, plan.smem_bytes, st);
     } else {  // a batch over groups of P CTAs
-      if (a.groups == 0 || a.groups > a.B || a.P > 32u) return cudaErrorInvalidValue;
+      if (a.groups == 0 || a.groups > a.B || a.P > 16u) return cudaErrorInvalidValue;
       if ((err = cudaMemsetAsync(a.gbar, 0, sizeof(uint32_t) * a.groups, st))) return err;
-      err = launch_rounds_m<kRoundT, true, kClusterCap, true>(a, m, plan.smem_bytes, st);
+      const int t = rounds_candidates_per_cta(a.P, a.max_pts);
+      err = t == kRoundTFew ? launch_rounds_m<kRoundTFew, true, kClusterCap, true>(a, m, plan.smem_bytes, st)
+            : t == kRoundTBig ? launch_rounds_m<kRoundTBig, true, kClusterCap, true>(a, m, plan.smem_bytes, st)
+                              : launch_rounds_m<kRoundT, true, kClusterCap, true>(a, m, plan.smem_bytes, st);
     }
   } else {
     if (a.P > (uint32_t)kMaxClusterP) return cudaErrorInvalidValue;
-    err = launch_rounds_m<kRoundT, false, kClusterCap>(a, plan.leaves_per_thread, plan.smem_bytes, st);
+    const int m = plan.leaves_per_thread;
+    const int t = rounds_candidates_per_cta(a.P, a.max_pts);
+    err = t == kRoundTFew ? launch_rounds_m<kRoundTFew, false, kClusterCap>(a, m, plan.smem_bytes, st)
+          : t == kRoundTBig ? launch_rounds_m<kRoundTBig, false, kClusterCap>(a, m, plan.smem_bytes, st)
+                            : launch_rounds_m<kRoundT, false, kClusterCap>(a, m, plan.smem_bytes, st);
   }
   launches += 1;
   return err;
