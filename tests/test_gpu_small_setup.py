@@ -6,10 +6,10 @@ per cloud in one launch (a single cloud) or two (a batch) instead of the ~25
 of the multi-launch pipeline.  Both must give the reference's bucket order,
 so the samples are compared index for index with the oracle, and the launch
 count shows which setup ran: sizes on both sides of each register-round step
-(4 / 8 / 10 / 16 / 24 x 1024 points; up to 10 x 1024 the cloud is staged
-in shared memory) and of the limit, exact distance ties, one bucket holding a whole cloud (runs cut every
-16 points), hashed grids (leaves with several cells) and a grid over the
-bucket limit.
+(4 / 8 / 10 / 16 / 24 x 1024 points; up to 10 x 1024 the cloud is staged in
+shared memory) and of the limit, exact distance ties, one bucket holding a
+whole cloud (runs cut every 16 points), hashed grids (leaves with several
+cells) and a grid over the bucket limit.
 """
 import numpy as np
 import pytest
