@@ -546,7 +546,6 @@ fps_rounds_cluster(const LoopArgs a) {
             __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
         const bool need = hit && lbd < lmax[m];
         u_ref += hit ? cnt[m] : 0u;
-        u_eval += need ? cnt[m] : 0u;
         needb[m] |= need ? (1u << j) : 0u;
       }
     }
@@ -572,6 +571,10 @@ fps_rounds_cluster(const LoopArgs a) {
         const uint32_t start = word & 0xffffu, c = (word >> 16) & 0xffu, nbits = word >> 24;
         const bool on = src >= 0 && (uint32_t)j16 < c;
         const uint32_t pi = start + (on ? (uint32_t)j16 : 0u);  // inside the leaf
+        // points evaluated: one per lane of the pass and sample it takes (the
+        // count in the leaf tests above cost the c3 / c4 / c5 loops 5-7 %)
+        if constexpr (kBatch == 1) u_eval += on ? 1u : 0u;
+        else u_eval += on ? (uint32_t)__popc(nbits) : 0u;
         const float4 p = s_pts[pi];
         float w = p.w;
 #pragma unroll
