@@ -383,7 +383,6 @@ fps_loop_cluster(const LoopArgs a) {
           __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
       need[m] = hit && lbd < lmax[m];
       u_ref += hit ? cnt[m] : 0u;
-      u_eval += need[m] ? cnt[m] : 0u;
     }
     // ---- (b) the warp updates the selected leaves together, two at a time:
     // half-warp h takes one leaf, lane j of the half its point j; each half's
@@ -407,6 +406,7 @@ fps_loop_cluster(const LoopArgs a) {
           const uint32_t lw = __float_as_uint(s_lo[l].w);
           const uint32_t start = lw & 0xffffu, c = lw >> 16;
           if ((uint32_t)j16 < c) {
+            ++u_eval;  // points evaluated, counted here rather than in the leaf tests
             float4 p = s_pts[start + j16];
             const float d = sqdist(p.x, p.y, p.z, q.x, q.y, q.z);
             if (d < p.w) { p.w = d; s_pts[start + j16].w = d; }
