@@ -93,3 +93,20 @@ def test_grid_over_bucket_limit_uses_pipeline():
     got, prof = _run(lambda: capi.fps(pts, 1000, bounds, blocks))
     np.testing.assert_array_equal(got, exp)
     assert prof.launches >= 12
+
+
+@pytest.mark.parametrize("n", [4096, 10000, 12288, 12289])
+def test_small_single_cloud_on_the_grid_loop(n):
+    """A single cloud of 4,096 points or more runs the 64-CTA grid-wide loop.
+    Up to 12,288 points it is launched right behind its setup with the
+    worst-case plan (every leaf a single point still leaves one leaf per
+    worker thread); above, after the plan's round trip.  Both exact."""
+    rs = np.random.RandomState(100 + n)
+    pts = _cloud(rs, n, n % 3)
+    bounds, blocks = (-4, 4, -4, 4, -4, 4), (16, 16, 16)
+    k = n // 8
+    exp = oracle.fps(pts, k, bounds, blocks)
+    for _ in range(2):  # the second call replays the cached setup graph
+        got, prof = _run(lambda: capi.fps(pts, k, bounds, blocks))
+        np.testing.assert_array_equal(got, exp)
+        assert prof.mode == 3 and prof.ctas_per_cloud == 64, (prof.mode, prof.ctas_per_cloud)
