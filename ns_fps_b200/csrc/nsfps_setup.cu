@@ -308,18 +308,20 @@ leaf_scatter(const uint32_t *__restrict__ run_start,
 
 // Leaf l = sorted points [s, e) of one bucket of range r: its bounding box,
 // the first maximum of d0 and the cell(s) whose cube membership selects it.
-__device__ __forceinline__ void build_leaf(uint32_t l, uint32_t s, uint32_t e, uint32_t bucket,
-                                           const RangeDev &r, const float4 *__restrict__ pts,
-                                           float4 *__restrict__ leaf_lo,
-                                           float4 *__restrict__ leaf_hi,
-                                           float *__restrict__ leaf_md,
-                                           uint32_t *__restrict__ leaf_pre) {
+// point(j) gives sorted point j as (x, y, z, d0).
+template <typename PointAt>
+__device__ __forceinline__ void build_leaf_of(uint32_t l, uint32_t s, uint32_t e, uint32_t bucket,
+                                              const RangeDev &r, PointAt point,
+                                              float4 *__restrict__ leaf_lo,
+                                              float4 *__restrict__ leaf_hi,
+                                              float *__restrict__ leaf_md,
+                                              uint32_t *__restrict__ leaf_pre) {
   float lx = FLT_MAX, ly = FLT_MAX, lz = FLT_MAX;
   float hx = -FLT_MAX, hy = -FLT_MAX, hz = -FLT_MAX;
   float md = -1.0f;
   uint32_t slot = 0;
   for (uint32_t j = s; j < e; ++j) {
-    const float4 p = pts[j];
+    const float4 p = point(j);
     lx = fminf(lx, p.x); ly = fminf(ly, p.y); lz = fminf(lz, p.z);
     hx = fmaxf(hx, p.x); hy = fmaxf(hy, p.y); hz = fmaxf(hz, p.z);
     if (p.w > md) { md = p.w; slot = j - s; }
@@ -352,6 +354,16 @@ __device__ __forceinline__ void build_leaf(uint32_t l, uint32_t s, uint32_t e, u
   leaf_lo[l] = make_float4(lx, ly, lz, __uint_as_float(cnt | (slot << 8) | (npre << 16)));
   leaf_hi[l] = make_float4(hx, hy, hz, __uint_as_float(cell0));
   leaf_md[l] = md;
+}
+
+__device__ __forceinline__ void build_leaf(uint32_t l, uint32_t s, uint32_t e, uint32_t bucket,
+                                           const RangeDev &r, const float4 *__restrict__ pts,
+                                           float4 *__restrict__ leaf_lo,
+                                           float4 *__restrict__ leaf_hi,
+                                           float *__restrict__ leaf_md,
+                                           uint32_t *__restrict__ leaf_pre) {
+  build_leaf_of(l, s, e, bucket, r, [&](uint32_t j) { return pts[j]; }, leaf_lo, leaf_hi, leaf_md,
+                leaf_pre);
 }
 
 __global__ void __launch_bounds__(256)
@@ -478,6 +490,30 @@ __device__ __forceinline__ void small_build_leaves(
     const uint32_t st = lstart[s + i], en = i + 1 < cnt ? lstart[s + i + 1] : e;
     leaf_start[L0 + i] = st;
     build_leaf(L0 + i, st, en, lbucket[s + i], r, pts, leaf_lo, leaf_hi, leaf_md, leaf_pre);
+  }
+}
+
+// small_build_leaves for a single cloud staged in shared memory: each point
+// from its sort word (buf, local sorted order) and the staged coordinates,
+// d0 recomputed exactly as the sorted points hold it, instead of a load from
+// global memory.
+__device__ __forceinline__ void small_build_leaves_staged(
+    uint32_t s, uint32_t e, uint32_t cnt, const RangeDev &r, const uint32_t *buf,
+    const float *s_xyz, float qx, float qy, float qz, const uint32_t *__restrict__ lstart,
+    const uint32_t *__restrict__ lbucket, uint32_t *__restrict__ leaf_start,
+    float4 *__restrict__ leaf_lo, float4 *__restrict__ leaf_hi, float *__restrict__ leaf_md,
+    uint32_t *__restrict__ leaf_pre) {
+  constexpr uint32_t kIdxMask = (1u << kSmallIdxBits) - 1u;
+  auto point = [&](uint32_t j) {
+    const uint32_t i = buf[j - s] & kIdxMask;
+    const float x = s_xyz[3 * i], y = s_xyz[3 * i + 1], z = s_xyz[3 * i + 2];
+    const float d = sqdist(x, y, z, qx, qy, qz);
+    return make_float4(x, y, z, (d < FLT_MAX) ? d : FLT_MAX);
+  };
+  for (uint32_t i = threadIdx.x; i < cnt; i += kSmallThreads) {
+    const uint32_t st = lstart[s + i], en = i + 1 < cnt ? lstart[s + i + 1] : e;
+    leaf_start[i] = st;
+    build_leaf_of(i, st, en, lbucket[s + i], r, point, leaf_lo, leaf_hi, leaf_md, leaf_pre);
   }
 }
 
@@ -710,8 +746,12 @@ small_sort(const float *__restrict__ xyz, const uint32_t *__restrict__ poff,
     leaf_start[total] = s + nc;
   }
   __syncthreads();  // lstart / lbucket / pts written above are visible to the CTA
-  small_build_leaves(c, 0u, total, r, pts, poff, lstart, lbucket, leaf_start, leaf_lo, leaf_hi,
-                     leaf_md, leaf_pre);
+  if (STAGE)
+    small_build_leaves_staged(s, s + nc, total, r, buf, s_xyz, qx, qy, qz, lstart, lbucket,
+                              leaf_start, leaf_lo, leaf_hi, leaf_md, leaf_pre);
+  else
+    small_build_leaves(c, 0u, total, r, pts, poff, lstart, lbucket, leaf_start, leaf_lo, leaf_hi,
+                       leaf_md, leaf_pre);
   small_plan(0u, total, leaf_lo, cand, ncand, plan, hist, buf);
 }
 
