@@ -708,8 +708,11 @@ small_sort(const float *__restrict__ xyz, const uint32_t *__restrict__ poff,
   }
 
   // leaves: runs of one bucket cut every kLeafSize points; thread t walks the
-  // sorted positions [t E, (t+1) E)
-  const uint32_t E = (nc + kSmallThreads - 1) / kSmallThreads;
+  // sorted positions [t E, (t+1) E).  A stride divisible by 4 puts a warp's
+  // reads of buf in at most 8 banks (E = 16: 2 banks, the c3 clouds' walk took
+  // 38 k cycles), so such an E is made odd.
+  uint32_t E = (nc + kSmallThreads - 1) / kSmallThreads;
+  if ((E & 3u) == 0u) E += 1u;
   const uint32_t p0 = min(nc, (uint32_t)tid * E), p1 = min(nc, p0 + E);
   auto run_mark = [&](uint32_t p) {
     return (p == 0 || (buf[p] >> kSmallIdxBits) != (buf[p - 1] >> kSmallIdxBits)) ? p : 0u;
