@@ -10,10 +10,11 @@ grown the per-device workspace of the allocating entry points.  It calls the
 C ABI directly and compares each result with the CPU oracle and with the
 allocating entry points (nsfps_fps_device and nsfps_fps) on the same
 device-resident input.  Sample indices are integers, so the tolerance is exact
-equality.  The cases cover a power-of-two grid (the round loop) and a
-non-power-of-two grid at the size limit (the per-step loop with its bucket
-preimage table: the largest layout the fixed array must hold), on the legacy
-default stream and on a separate stream.
+equality.  The cases cover power-of-two grids (the round loop: a small cloud
+set up by one CTA and launched without a plan round trip, a mid-size one and
+one at the size limit) and a non-power-of-two grid at the size limit (the
+per-step loop with its bucket preimage table: the largest layout the fixed
+array must hold), on the legacy default stream and on a separate stream.
 """
 import numpy as np
 import pytest
@@ -53,10 +54,12 @@ def _via_static(capi, d, n, k, bounds, blocks, out, stream=None):
 
 
 def _cases():
+    s = synthetic.gaussian_cloud(10_000, seed=10)
     a = synthetic.gaussian_cloud(20_000, seed=11)
     b = synthetic.sphere_cube_cloud(STATIC_MAX_POINTS, seed=12)
     c = synthetic.gaussian_cloud(STATIC_MAX_POINTS, seed=14)
-    return [(a, 2_000, (16, 16, 16)), (b, 4_096, (32, 32, 32)), (c, 3_000, (20, 20, 20))]
+    return [(s, 1_000, (16, 16, 16)), (a, 2_000, (16, 16, 16)), (b, 4_096, (32, 32, 32)),
+            (c, 3_000, (20, 20, 20))]
 
 
 def test_static_matches_oracle_and_allocating_entry_points_two_calls(capi):
