@@ -70,7 +70,7 @@ def fps(points, k, bounds=None, blocks=(16, 16, 16), device=0):
     nsfps_fps_with_bbox otherwise (fps_with_bbox)."""
     p = np.ascontiguousarray(np.asarray(points, dtype=np.float32))
     n = p.shape[0]
-    out = np.zeros(max(min(int(k), n), 1), dtype=np.uint64)
+    out = np.empty(max(min(int(k), n), 1), dtype=np.uint64)  # the library fills [0, len)
     ln = ctypes.c_uint64(0)
     if bounds is None and tuple(int(b) for b in blocks) != (16, 16, 16):
         xb, yb, zb = (int(b) for b in blocks)
@@ -81,14 +81,19 @@ def fps(points, k, bounds=None, blocks=(16, 16, 16), device=0):
                                        ctypes.c_int(device))
         if rc != OK:
             raise RuntimeError(f"nsfps_fps_with_bbox rc={rc}: {last_error()}")
-        return out[:ln.value].copy()
+        return _trimmed(out, ln.value)
     r = rng(bounds, blocks) if bounds is not None else None
     rc = lib().nsfps_fps(p.ctypes.data_as(_f32p), ctypes.c_uint64(n), ctypes.c_uint64(int(k)),
                          ctypes.byref(r) if r is not None else None,
                          out.ctypes.data_as(_u64p), ctypes.byref(ln), ctypes.c_int(device))
     if rc != OK:
         raise RuntimeError(f"nsfps_fps rc={rc}: {last_error()}")
-    return out[:ln.value].copy()
+    return _trimmed(out, ln.value)
+
+
+def _trimmed(out, n):
+    """The first n entries: the array itself when full, else a compact copy."""
+    return out if n == out.shape[0] else out[:n].copy()
 
 
 def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
@@ -96,7 +101,11 @@ def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
     cnt = len(cl)
     ptrs = (_f32p * cnt)(*[c.ctypes.data_as(_f32p) for c in cl])
     ns = (ctypes.c_uint64 * cnt)(*[c.shape[0] for c in cl])
-    outs = [np.zeros(max(min(int(k), c.shape[0]), 1), dtype=np.uint64) for c in cl]
+    # one block for every cloud's samples (the library fills each one's head)
+    caps = [max(min(int(k), c.shape[0]), 1) for c in cl]
+    starts = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
+    block = np.empty(int(starts[-1]), dtype=np.uint64)
+    outs = [block[starts[i]:starts[i + 1]] for i in range(cnt)]
     optrs = (_u64p * cnt)(*[o.ctypes.data_as(_u64p) for o in outs])
     lens = (ctypes.c_uint64 * cnt)()
     if per_cloud:
@@ -109,7 +118,7 @@ def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
                                  ctypes.c_int(len(devices)))
     if rc != OK:
         raise RuntimeError(f"nsfps_fps_batched rc={rc}: {last_error()}")
-    return [o[:lens[i]].copy() for i, o in enumerate(outs)]
+    return [o[:lens[i]] for i, o in enumerate(outs)]
 
 
 class TestHooks(ctypes.Structure):

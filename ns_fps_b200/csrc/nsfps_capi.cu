@@ -639,7 +639,7 @@ int small_setup(const Job &j, const uint32_t *cand, int ncand) {
 // Writes B*k uint64 results to d_out and the B lengths to lens (host).
 int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_packed,
             const float *const *h_clouds, const float *d_xyz_in, uint64_t *d_out_user,
-            std::vector<uint32_t> &lens, std::vector<uint64_t> *h_out) {
+            std::vector<uint32_t> &lens, const uint64_t **h_out) {
   const bool own_xyz = d_xyz_in == nullptr;
   const bool own_out = d_out_user == nullptr;
   Buffers b{};
@@ -672,9 +672,14 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   const int ncand = j.B == 1 ? kNumSingle : kNumBatch;
   const ParamLayout L = param_layout(j);
   const size_t cbytes = ctrl_bytes(j);
-  unsigned char *hs = staging(ctx, std::max(L.bytes, cbytes));
+  // (with host results: they come back behind the control block, so one
+  // pinned buffer takes both and the copy runs asynchronously)
+  const size_t res_off = align_up(cbytes, 256);
+  const size_t res_bytes = h_out ? sizeof(uint64_t) * j.B * (size_t)j.k : 0;
+  const size_t sbytes = std::max(L.bytes, res_off + res_bytes);
+  unsigned char *hs = staging(ctx, sbytes);
   if (!hs) return set_error(NSFPS_ERR_OOM, "host staging buffer of %zu bytes unavailable",
-                            std::max(L.bytes, cbytes));
+                            sbytes);
   std::memcpy(hs + L.poff, j.poff.data(), 4 * ((size_t)j.B + 1));
   std::memcpy(hs + L.rid, j.rid.data(), 4 * (size_t)j.B);
   std::memcpy(hs + L.boff, j.boff.data(), 4 * (size_t)j.B);
@@ -905,9 +910,8 @@ int run_job(DeviceCtx *ctx, cudaStream_t st, const Job &j, const float *h_xyz_pa
   unsigned long long hstats[4] = {};
   NSFPS_CUDA(cudaMemcpyAsync(hs, b.ctrl, cbytes, cudaMemcpyDeviceToHost, st));
   if (h_out) {
-    h_out->resize((size_t)j.B * j.k);
-    NSFPS_CUDA(cudaMemcpyAsync(h_out->data(), d_out, sizeof(uint64_t) * j.B * (size_t)j.k,
-                               cudaMemcpyDeviceToHost, st));
+    NSFPS_CUDA(cudaMemcpyAsync(hs + res_off, d_out, res_bytes, cudaMemcpyDeviceToHost, st));
+    *h_out = reinterpret_cast<const uint64_t *>(hs + res_off);
   }
   NSFPS_CUDA(cudaStreamSynchronize(st));
   std::memcpy(hscal, hs + kCtrlScalars, sizeof(hscal));
@@ -1194,7 +1198,9 @@ int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
   rc = build_job(gn.data(), gn.size(), k, ranges, grid, j);
   if (rc) return rc;
   std::vector<uint32_t> lens;
-  std::vector<uint64_t> hout;
+  // the results stay in the device's staging buffer until the next call,
+  // which the device lock held here keeps out
+  const uint64_t *hout = nullptr;
   rc = run_job(ctx, ctx->stream, j, nullptr, gc.data(), nullptr, nullptr, lens, &hout);
   if (rc == NSFPS_ERR_UNSUPPORTED && gpu_idx.size() > 1) {
     // a cloud too large to share the device with the others: one job per
@@ -1206,7 +1212,7 @@ int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
       rc = run_job(ctx, ctx->stream, j1, nullptr, &gc[c], nullptr, nullptr, lens, &hout);
       if (rc) return rc;
       const uint64_t i = gpu_idx[c];
-      std::memcpy(out[i], hout.data(), sizeof(uint64_t) * lens[0]);
+      std::memcpy(out[i], hout, sizeof(uint64_t) * lens[0]);
       out_len[i] = lens[0];
     }
     return NSFPS_OK;
@@ -1214,7 +1220,7 @@ int batched_on_device(int device, const float *const *clouds, const uint64_t *n,
   if (rc) return rc;
   for (size_t c = 0; c < gpu_idx.size(); ++c) {
     const uint64_t i = gpu_idx[c];
-    std::memcpy(out[i], hout.data() + c * (size_t)k, sizeof(uint64_t) * lens[c]);
+    std::memcpy(out[i], hout + c * (size_t)k, sizeof(uint64_t) * lens[c]);
     out_len[i] = lens[c];
   }
   return NSFPS_OK;
