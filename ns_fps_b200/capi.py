@@ -99,14 +99,16 @@ def _trimmed(out, n):
 def fps_batched(clouds, k, bounds, blocks, devices=(0,), per_cloud=False):
     cl = [np.ascontiguousarray(np.asarray(c, dtype=np.float32)) for c in clouds]
     cnt = len(cl)
-    ptrs = (_f32p * cnt)(*[c.ctypes.data_as(_f32p) for c in cl])
+    # pointer arrays from plain addresses (ctypes.data_as costs microseconds
+    # per array)
+    ptrs = (ctypes.c_void_p * cnt)(*[c.ctypes.data for c in cl])
     ns = (ctypes.c_uint64 * cnt)(*[c.shape[0] for c in cl])
     # one block for every cloud's samples (the library fills each one's head)
     caps = [max(min(int(k), c.shape[0]), 1) for c in cl]
     starts = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
     block = np.empty(int(starts[-1]), dtype=np.uint64)
     outs = [block[starts[i]:starts[i + 1]] for i in range(cnt)]
-    optrs = (_u64p * cnt)(*[o.ctypes.data_as(_u64p) for o in outs])
+    optrs = (ctypes.c_void_p * cnt)(*[o.ctypes.data for o in outs])
     lens = (ctypes.c_uint64 * cnt)()
     if per_cloud:
         rs = (Range * cnt)(*[rng(b, bl) for b, bl in zip(bounds, blocks)])
