@@ -1240,15 +1240,16 @@ cudaError_t launch_rounds_m(const LoopArgs &a, int m, size_t smem, cudaStream_t 
   }
 }
 
-// Grid-wide rounds over P = 64 or 128 CTAs publish 6 or 4 candidates per
-// CTA (384 or 512 in all).  The round lasts while the best candidate beats
+// Grid-wide rounds over P = 64 or 128 CTAs publish 5 or 4 candidates per
+// CTA (320 or 512 in all).  The round lasts while the best candidate beats
 // the largest CTA bound; more candidates per CTA lower that bound but cost
-// every step more work: on c2 (P = 64) 4, 6 and 8 per CTA gave 4.160, 4.149
-// and 4.19 ms, on c4 (P = 128) 4 per CTA gave 28.4 ms against 32.2 for 2.
+// every step more work: on c2 (P = 64) 4 / 5 / 6 / 7 / 8 per CTA gave 4.218 /
+// 4.050 / 4.087 / 4.070 / 4.186 ms (bit-identical samples), on c4 (P = 128) 4
+// per CTA gave 28.4 ms against 32.2 for 2.
 // Groups of at most 16 CTAs (batches) publish as a cluster does (at most
 // big_t(P) each).
 constexpr int grid_t(uint32_t P) {
-  return P == 64u ? 6 : (P == 128u ? 4 : (P <= 16u ? big_t(P) : 0));
+  return P == 64u ? 5 : (P == 128u ? 4 : (P <= 16u ? big_t(P) : 0));
 }
 constexpr int grid_cap(uint32_t P) { return P == 64u || P == 128u ? (int)P * grid_t(P) : kClusterCap; }
 static_assert(16 * kRoundT <= kClusterCap && 16 * kRoundTBig <= kClusterCap &&

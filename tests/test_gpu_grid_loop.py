@@ -2,7 +2,7 @@
 oracle: bit-exact indices.
 
 * The grid-wide loop (one cloud of at least 4,096 points over 64 or 128
-  co-resident CTAs, 384 or 512 published candidates per round) on seeded
+  co-resident CTAs, 320 or 512 published candidates per round) on seeded
   random clouds: the golden vectors pin it on the c2 and c4 configs only;
   these cases add exact distance ties (quantised coordinates), clamped
   outliers (ranges narrower than the data), clustered and flat clouds and
