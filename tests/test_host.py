@@ -88,6 +88,25 @@ def test_reference_early_returns_need_no_gpu():
     assert np.array_equal(capi.fps(pts, 100, None), np.arange(7))
 
 
+def test_batched_wrapper_returns_each_clouds_samples_without_gpu():
+    """The batched wrapper hands the library one output block and returns a
+    view per cloud; clouds the reference answers without sampling (k >= n,
+    n == 0) exercise it on the host."""
+    rs = np.random.RandomState(1)
+    clouds = [rs.randn(n, 3).astype(np.float32) for n in (3, 0, 12, 1)]
+    got = capi.fps_batched(clouds, 12, (-5, 5, -5, 5, -5, 5), (4, 4, 4))
+    assert [len(g) for g in got] == [3, 0, 12, 1]
+    for g, c in zip(got, clouds):
+        assert g.dtype == np.uint64
+        np.testing.assert_array_equal(g, np.arange(c.shape[0]))
+    # the views do not overlap: writing one leaves the others intact
+    got[0][:] = 7
+    np.testing.assert_array_equal(got[2], np.arange(12))
+    # the single-cloud wrapper returns the full array itself, or a compact copy
+    full = capi.fps(clouds[2], 12, (-5, 5, -5, 5, -5, 5), (4, 4, 4))
+    assert full.flags.owndata and len(full) == 12
+
+
 def _rc_of_fps(pts, k, bounds, blocks):
     p = np.ascontiguousarray(pts, dtype=np.float32)
     out = np.zeros(max(k, 1), dtype=np.uint64)
